@@ -1,0 +1,179 @@
+/*
+ * b200ops.h -- C-ABI of libb200ops.so, the sm_100a kernels behind the
+ * tensor-parallel Qwen3 decoder forward path of nano-vllm-diy.
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless stated otherwise; tensors are
+ *     bf16 ("void*"), int32 (block tables, cu_seqlens, slot mapping) or int64
+ *     (token ids, positions) as documented per argument.
+ *   - Strides are in ELEMENTS between consecutive rows (tokens).
+ *   - Calls launch on `stream` and return immediately; nothing is allocated
+ *     and nothing synchronises, so every call can be captured in a CUDA graph.
+ *   - Return value: B200_OK (0) or a negative status; b200_last_error()
+ *     returns the message of the calling thread's last failure.
+ *   - Kernels never trap.  Out-of-range slot / block-table entries and
+ *     timed-out waits set bits of a per-device error word instead, readable
+ *     with b200_device_error() (which synchronises the device).
+ *
+ * Reference interfaces are cited as path:line inside DestineG/nano-vllm-diy.
+ */
+#ifndef B200OPS_H_
+#define B200OPS_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_ABI_VERSION 1
+
+#define B200_OK 0
+#define B200_ERR_INVALID (-1)     /* bad shape, stride, alignment or null pointer */
+#define B200_ERR_UNSUPPORTED (-2) /* shape outside what the kernels implement */
+#define B200_ERR_CUDA (-3)        /* a CUDA runtime / driver call failed */
+#define B200_ERR_WORKSPACE (-4)   /* caller-provided workspace too small */
+#define B200_ERR_PEER (-5)        /* tensor-parallel communicator not set up */
+
+/* device error word bits (b200_device_error) */
+#define B200_DEVERR_MBAR_TIMEOUT 1u
+#define B200_DEVERR_PEER_TIMEOUT 2u
+#define B200_DEVERR_BAD_INDEX 4u
+
+typedef struct CUstream_st* b200_stream_t; /* == cudaStream_t */
+
+const char* b200_last_error(void);
+int b200_version(void);
+
+/* Reads the device error word of the current device; clears it when `clear`
+ * is non-zero.  Synchronous. */
+int b200_device_error(unsigned* out, int clear);
+
+/* ------------------------------------------------------------------------
+ * Linear layers
+ * ------------------------------------------------------------------------ */
+
+/* Bytes of fp32 split-K workspace b200_linear would use for this shape
+ * (0 when it does not split K).  A smaller workspace is allowed: the kernel
+ * then splits less. */
+int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes);
+
+/* y[T, N] = x[T, K] * w[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate,
+ * tcgen05 tensor cores.  Replaces F.linear in
+ *   src/layers/linear.py:74-75   ColumnParallelLinear.forward
+ *   src/layers/linear.py:169-170 RowParallelLinear.forward (per-rank part)
+ *   src/layers/llm_head.py:64    ParallelLMHead.forward
+ * K, ldx and ldw must be multiples of 8; x and w 16-byte aligned. */
+int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
+                void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
+                b200_stream_t stream);
+
+/* y[T, I] = silu(x * w[:I]^T) * (x * w[I:]^T): the gate_up projection with
+ * SiLU-and-mul in its epilogue.  Replaces
+ *   src/models/qwen3.py:119-121 (gate_up_proj -> act_fn) =
+ *   src/layers/linear.py:74-75 + src/layers/activation.py:6-10.
+ * w is [2I, K] with rows [gate ; up] exactly as MergedColumnParallelLinear
+ * stores them (src/layers/linear.py:89-102). */
+int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long long ldw, void* y,
+                             long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
+                             b200_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Normalisation, RoPE, activation
+ * ------------------------------------------------------------------------ */
+
+/* RMSNorm over rows of `dim` (multiple of 8, <= 8192).
+ * residual == NULL: out = bf16(w * (x / sqrt(mean(x^2) + eps)))
+ *   -> src/layers/layernorm.py:10-16 RMSNorm.normal_forward
+ * residual != NULL: s = x + residual (fp32); residual_out = bf16(s);
+ *   out = bf16(w * (s / sqrt(mean(s^2) + eps)))
+ *   -> src/layers/layernorm.py:18-28 RMSNorm.residual_forward
+ * residual and residual_out are contiguous [rows, dim]; they may alias. */
+int b200_rms_norm(const void* x, long long x_stride, const void* residual, const void* weight,
+                  void* out, long long out_stride, void* residual_out, int rows, int dim,
+                  float eps, b200_stream_t stream);
+
+/* Per token: q heads -> RMSNorm(q_norm_w) -> RoPE -> q_out;
+ * k heads -> RMSNorm(k_norm_w) -> RoPE -> k_out and k_cache[slot];
+ * v heads -> v_out and v_cache[slot].  head_dim is 128.
+ * Replaces src/models/qwen3.py:81-89 (split, q_norm/k_norm, rotary_emb)
+ * together with the cache write of src/layers/attention.py:86-88.
+ *  - q_norm_w / k_norm_w NULL: no q/k norm (attention_bias models,
+ *    src/models/qwen3.py:85).
+ *  - v_in NULL: RoPE only (src/layers/pos_embedding.py:30-52 RoPE.forward).
+ *  - k_cache NULL: no cache write; otherwise slot_mapping[t] == -1 skips t.
+ *  - cos_sin: fp32 [max_pos, 128] = [cos | sin] table of
+ *    src/layers/pos_embedding.py:6-18; positions: int64 [T].
+ *  - k_out / v_out may be NULL. */
+int b200_qk_norm_rope_store(const void* q_in, long long q_in_stride, const void* k_in,
+                            long long k_in_stride, const void* v_in, long long v_in_stride, int T,
+                            int Hq, int Hkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                            const float* cos_sin, long long max_pos, const long long* positions,
+                            const int* slot_mapping, void* k_cache, void* v_cache,
+                            long long num_slots, void* q_out, void* k_out, void* v_out,
+                            b200_stream_t stream);
+
+/* out[T, I] = silu(x[:, :I]) * x[:, I:].
+ * Replaces src/layers/activation.py:6-10 SiluAndMul.forward. */
+int b200_silu_and_mul(const void* x, long long x_stride, void* out, long long out_stride, int T,
+                      int I, b200_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * KV cache and attention
+ * ------------------------------------------------------------------------ */
+
+/* k_cache.view(-1, D)[slot_mapping[i]] = key[i] (and value), slot -1 skipped,
+ * 16-byte vector copies; slot_mapping is int32 [T]; num_slots bounds the
+ * cache rows (num_blocks * block_size).
+ * Replaces src/layers/attention.py:36-61 store_kvcache (Triton kernel
+ * store_kvcache_kernel, src/layers/attention.py:10-34). */
+int b200_store_kvcache(const void* key, long long key_stride, const void* value,
+                       long long value_stride, void* k_cache, void* v_cache,
+                       const int* slot_mapping, int T, int D, long long num_slots,
+                       b200_stream_t stream);
+
+/* Workspace of b200_paged_attention's decode path for up to `max_seqs`
+ * sequences of up to `max_seqlen_k` keys. */
+int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_t* bytes);
+
+/* Causal (bottom-right aligned) varlen GQA attention, head_dim 128.
+ * Replaces src/layers/attention.py:93-104 (flash_attn_varlen_func with
+ * cu_seqlens_q/k, max_seqlen_q/k, softmax_scale, causal=True, block_table).
+ *  - block_tables != NULL: K/V from the paged cache [num_blocks, page, Hkv,
+ *    128] (int32 block_tables: B rows of bt_width entries, bt_stride apart,
+ *    -1 padded; a key past the row's width or in a -1 block is read as zero
+ *    and flags B200_DEVERR_BAD_INDEX);
+ *    block_tables == NULL: K/V from contiguous k / v rows cu_seqlens_k[b]+j.
+ *  - cu_seqlens_q / cu_seqlens_k: int32 [B + 1] on the device; sequences
+ *    with q length <= 0 (CUDA-graph padding) are skipped.
+ *  - max_seqlen_q == 1 with a block table takes the split-KV decode kernel
+ *    and needs `workspace` (b200_attention_workspace_bytes); max_seqlen_k
+ *    only bounds the launch. */
+int b200_paged_attention(const void* q, long long q_stride, const void* k, long long k_stride,
+                         const void* v, long long v_stride, const void* k_cache,
+                         const void* v_cache, long long num_slots, const int* block_tables,
+                         int bt_stride, int bt_width, const int* cu_seqlens_q, const int* cu_seqlens_k, int B,
+                         int max_seqlen_q, int max_seqlen_k, int Hq, int Hkv, int page,
+                         float softmax_scale, void* out, long long out_stride, void* workspace,
+                         size_t ws_bytes, b200_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Vocabulary
+ * ------------------------------------------------------------------------ */
+
+/* out[t] = weight[ids[t] - vocab_start] if vocab_start <= ids[t] < vocab_end
+ * else 0 (int64 ids).  The local half of src/layers/llm_head.py:38-49
+ * VocabParallelEmbedding.forward (the all_reduce stays in NCCL). */
+int b200_embedding(const long long* ids, const void* weight, void* out, int T, int H,
+                   long long vocab_start, long long vocab_end, b200_stream_t stream);
+
+/* out[r] = argmax(logits[r, :V]) (first maximum), int64.  Greedy selection
+ * over the logits returned by src/layers/llm_head.py:60-69. */
+int b200_argmax(const void* logits, long long stride, int rows, int V, long long* out,
+                b200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200OPS_H_ */

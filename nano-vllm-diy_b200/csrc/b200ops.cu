@@ -1,0 +1,475 @@
+// C-ABI of the B200 decoder-path kernels (libb200ops.so).
+//
+// Every entry point takes raw device pointers, sizes and a cudaStream_t,
+// allocates nothing, launches on the given stream (so it can be captured in a
+// CUDA graph) and returns B200_OK or a negative status.  The message of the
+// last failure on the calling thread is available from b200_last_error().
+// Declarations and the reference interface each one replaces are in
+// include/b200ops.h.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "elementwise.cuh"
+#include "gemm.cuh"
+#include "../../include/b200ops.h"
+
+using namespace b200;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return B200_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+// Per-device state: SM count, the device error word's address and which
+// kernels already had their dynamic shared memory limit raised.
+struct DeviceState {
+  bool init = false;
+  int num_sms = 0;
+  unsigned* err = nullptr;
+  unsigned smem_configured = 0;
+};
+DeviceState g_dev[kMaxDevices];
+
+__device__ unsigned g_device_error_word;
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(B200_ERR_INVALID, "device %d out of range", dev);
+  DeviceState& s = g_dev[dev];
+  if (!s.init) {
+    e = cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return fail(B200_ERR_CUDA, "SM count: %s", cudaGetErrorString(e));
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_device_error_word);
+    if (e != cudaSuccess) return fail(B200_ERR_CUDA, "error word: %s", cudaGetErrorString(e));
+    s.err = static_cast<unsigned*>(p);
+    s.init = true;
+  }
+  *out = &s;
+  return B200_OK;
+}
+
+template <typename K>
+int ensure_smem(DeviceState* ds, unsigned bit, K kernel, int bytes) {
+  if (ds->smem_configured & bit) return B200_OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "smem attribute: %s", cudaGetErrorString(e));
+  (void)bytes;
+  ds->smem_configured |= bit;
+  return B200_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map: `rows` rows of `inner` elements, `row_stride` elements
+// apart, box = box_inner x box_rows, 128-byte swizzle, zero fill outside.
+int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+              uint64_t row_stride, uint32_t box_inner, uint32_t box_rows) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride * 2};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return B200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// GEMM planning
+// ---------------------------------------------------------------------------
+struct GemmPlan {
+  int BN, token_tiles, n_tiles, num_kb, kb_per_split, splits, stages, smem, tmem_cols;
+};
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+GemmPlan plan_gemm(int T, int N, int K, bool silu_tiles, int num_sms, size_t ws_bytes,
+                   int ws_cols) {
+  GemmPlan p{};
+  p.BN = T <= 256 ? max(32, round_up(T, 32)) : 256;
+  p.token_tiles = (T + p.BN - 1) / p.BN;
+  p.n_tiles = silu_tiles ? (N / 2 + 63) / 64 : (N + kGemmBM - 1) / kGemmBM;
+  p.num_kb = (K + kGemmBK - 1) / kGemmBK;
+  const int tiles = p.n_tiles * p.token_tiles;
+  int splits = 1;
+  if (tiles < num_sms) {
+    splits = min(p.num_kb, (2 * num_sms + tiles - 1) / tiles);
+    // every split must own at least 4 K blocks
+    splits = max(1, min(splits, p.num_kb / 4));
+    // and the fp32 partials must fit the caller's workspace
+    while (splits > 1 && (size_t)splits * T * ws_cols * sizeof(float) > ws_bytes) --splits;
+  }
+  p.kb_per_split = (p.num_kb + splits - 1) / splits;
+  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  const int stage = kGemmBM * kGemmBK * 2 + p.BN * kGemmBK * 2;
+  p.stages = max(2, min(kGemmMaxStages, (100 * 1024) / stage));
+  p.smem = p.stages * stage + 1024 + 256;
+  p.tmem_cols = 32;
+  while (p.tmem_cols < p.BN) p.tmem_cols <<= 1;
+  return p;
+}
+
+int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const void* bias, void* y,
+             long long ldy, int T, int N, int K, bool silu, void* ws, size_t ws_bytes,
+             cudaStream_t st) {
+  if (T <= 0) return B200_OK;
+  if (N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "linear: bad shape N=%d K=%d", N, K);
+  if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K)
+    return fail(B200_ERR_INVALID, "linear: K (%d) and row strides (%lld, %lld) must be multiples of 8", K, ldx, ldw);
+  if (!aligned16(x) || !aligned16(w)) return fail(B200_ERR_INVALID, "linear: x and w must be 16-byte aligned");
+  if (silu && (N % 2 || ldy < N / 2)) return fail(B200_ERR_INVALID, "linear_silu: bad N=%d / ldy", N);
+  if (!silu && ldy < N) return fail(B200_ERR_INVALID, "linear: ldy < N");
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  GemmPlan p = plan_gemm(T, N, K, silu && (N / 2) % 64 == 0, ds->num_sms, ws ? ws_bytes : 0, N);
+  const bool fused_silu = silu && p.splits == 1 && (N / 2) % 64 == 0;
+  if (silu && !fused_silu) {
+    // silu via fp32 partials + reduce: plan over all N rows of W
+    p = plan_gemm(T, N, K, false, ds->num_sms, ws ? ws_bytes : 0, N);
+    if ((size_t)p.splits * T * N * sizeof(float) > ws_bytes || ws == nullptr) {
+      // force a single split through the reduce path
+      p.kb_per_split = p.num_kb;
+      p.splits = 1;
+      if ((size_t)T * N * sizeof(float) > ws_bytes || ws == nullptr)
+        return fail(B200_ERR_WORKSPACE, "linear_silu: workspace of %zu bytes too small (need %zu)",
+                    ws_bytes, (size_t)T * N * sizeof(float));
+    }
+  }
+  if (ws != nullptr && !aligned16(ws)) return fail(B200_ERR_INVALID, "linear: workspace must be 16-byte aligned");
+  CUtensorMap tmW, tmX;
+  if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK,
+                        fused_silu ? 64u : (uint32_t)kGemmBM))
+    return r;
+  if (int r = make_tmap(&tmX, x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx, kGemmBK, (uint32_t)p.BN))
+    return r;
+  if (int r = ensure_smem(ds, 1u, gemm_tn_tcgen05_kernel, p.smem)) return r;
+  GemmArgs a{};
+  a.T = T; a.N = N; a.K = K; a.BN = p.BN; a.stages = p.stages; a.num_kb = p.num_kb;
+  a.kb_per_split = p.kb_per_split; a.tmem_cols = p.tmem_cols;
+  a.y = static_cast<__nv_bfloat16*>(y); a.ldy = ldy;
+  a.ws = static_cast<float*>(ws);
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.silu_inter = N / 2;
+  a.err = ds->err;
+  const bool reduce = p.splits > 1 || (silu && !fused_silu);
+  a.epi = fused_silu ? EPI_SILU : (reduce ? EPI_F32 : EPI_BF16);
+  dim3 grid(p.n_tiles, p.token_tiles, p.splits);
+  gemm_tn_tcgen05_kernel<<<grid, kGemmThreads, p.smem, st>>>(tmW, tmX, a);
+  if (int r = check_launch("gemm_tn_tcgen05_kernel")) return r;
+  if (reduce) {
+    const int outN = silu ? N / 2 : N;
+    const long long vecs = (long long)T * (outN / 4);
+    const int blocks = (int)std::min<long long>((vecs + 255) / 256, (long long)ds->num_sms * 8);
+    splitk_reduce_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(ws), p.splits, T, N,
+                                                 static_cast<__nv_bfloat16*>(y), ldy,
+                                                 static_cast<const __nv_bfloat16*>(bias),
+                                                 silu ? EPI_SILU : EPI_BF16);
+    if (int r = check_launch("splitk_reduce_kernel")) return r;
+  }
+  return B200_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// exported C-ABI
+// ===========================================================================
+extern "C" {
+
+const char* b200_last_error(void) { return g_last_error.c_str(); }
+
+int b200_version(void) { return B200_ABI_VERSION; }
+
+int b200_device_error(unsigned* out, int clear) {
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpy(&v, ds->err, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "read error word: %s", cudaGetErrorString(e));
+  if (clear) {
+    const unsigned z = 0;
+    e = cudaMemcpy(ds->err, &z, sizeof(z), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return fail(B200_ERR_CUDA, "clear error word: %s", cudaGetErrorString(e));
+  }
+  if (out) *out = v;
+  return B200_OK;
+}
+
+int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes) {
+  if (!bytes || T < 0 || N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "bad arguments");
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  const GemmPlan p = plan_gemm(T, N, K, false, ds->num_sms, (size_t)-1 / 2, N);
+  *bytes = p.splits > 1 ? (size_t)p.splits * T * N * sizeof(float) : 0;
+  return B200_OK;
+}
+
+int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
+                void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
+                b200_stream_t stream) {
+  return run_gemm(x, ldx, w, ldw, bias, y, ldy, T, N, K, false, workspace, ws_bytes,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long long ldw, void* y,
+                             long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
+                             b200_stream_t stream) {
+  return run_gemm(x, ldx, w, ldw, nullptr, y, ldy, T, 2 * I, K, true, workspace, ws_bytes,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+int b200_rms_norm(const void* x, long long x_stride, const void* residual, const void* weight,
+                  void* out, long long out_stride, void* residual_out, int rows, int dim, float eps,
+                  b200_stream_t stream) {
+  if (rows <= 0) return B200_OK;
+  if (dim <= 0 || dim % 8 || dim > 8 * 256 * 4)
+    return fail(B200_ERR_UNSUPPORTED, "rms_norm: dim %d must be a multiple of 8 and <= 8192", dim);
+  if (x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(out) || !aligned16(weight))
+    return fail(B200_ERR_INVALID, "rms_norm: rows must be 16-byte aligned");
+  if (residual && (!residual_out || !aligned16(residual) || !aligned16(residual_out)))
+    return fail(B200_ERR_INVALID, "rms_norm: residual needs an aligned residual_out");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int nvec = dim / 8;
+  const int threads = nvec >= 256 ? 256 : max(32, round_up(nvec, 32));
+  const int vpt = (nvec + threads - 1) / threads;
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto R = static_cast<const __nv_bfloat16*>(residual);
+  auto W = static_cast<const __nv_bfloat16*>(weight);
+  auto O = static_cast<__nv_bfloat16*>(out);
+  auto RO = static_cast<__nv_bfloat16*>(residual_out);
+#define B200_LAUNCH_NORM(V)                                                                      \
+  do {                                                                                           \
+    if (residual)                                                                                \
+      rms_norm_kernel<V, true><<<rows, threads, 0, st>>>(X, x_stride, R, W, O, out_stride, RO,   \
+                                                          dim, eps);                             \
+    else                                                                                         \
+      rms_norm_kernel<V, false><<<rows, threads, 0, st>>>(X, x_stride, R, W, O, out_stride, RO,  \
+                                                           dim, eps);                            \
+  } while (0)
+  if (vpt <= 1) B200_LAUNCH_NORM(1);
+  else if (vpt <= 2) B200_LAUNCH_NORM(2);
+  else B200_LAUNCH_NORM(4);
+#undef B200_LAUNCH_NORM
+  return check_launch("rms_norm_kernel");
+}
+
+int b200_qk_norm_rope_store(const void* q_in, long long q_in_stride, const void* k_in,
+                            long long k_in_stride, const void* v_in, long long v_in_stride, int T,
+                            int Hq, int Hkv, const void* q_norm_w, const void* k_norm_w, float eps,
+                            const float* cos_sin, long long max_pos, const long long* positions,
+                            const int* slot_mapping, void* k_cache, void* v_cache,
+                            long long num_slots, void* q_out, void* k_out, void* v_out,
+                            b200_stream_t stream) {
+  if (T <= 0) return B200_OK;
+  if (Hq <= 0 || Hkv <= 0 || !q_in || !k_in || !q_out || !cos_sin || !positions)
+    return fail(B200_ERR_INVALID, "qk_norm_rope_store: missing argument");
+  if ((q_in_stride | k_in_stride | v_in_stride) % 2)
+    return fail(B200_ERR_INVALID, "qk_norm_rope_store: strides must be even");
+  if (k_cache && (!v_cache || !slot_mapping || !v_in))
+    return fail(B200_ERR_INVALID, "qk_norm_rope_store: cache store needs v, v_cache and slot_mapping");
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  QKNormRopeArgs a{};
+  a.q_in = static_cast<const __nv_bfloat16*>(q_in);
+  a.k_in = static_cast<const __nv_bfloat16*>(k_in);
+  a.v_in = static_cast<const __nv_bfloat16*>(v_in);
+  a.q_in_stride = q_in_stride; a.k_in_stride = k_in_stride; a.v_in_stride = v_in_stride;
+  a.T = T; a.Hq = Hq; a.Hkv = Hkv;
+  a.q_w = static_cast<const __nv_bfloat16*>(q_norm_w);
+  a.k_w = static_cast<const __nv_bfloat16*>(k_norm_w);
+  a.eps = eps; a.cos_sin = cos_sin; a.positions = positions; a.max_pos = max_pos;
+  a.slot_mapping = slot_mapping;
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.num_slots = num_slots;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_out = static_cast<__nv_bfloat16*>(k_out);
+  a.v_out = static_cast<__nv_bfloat16*>(v_out);
+  a.err = ds->err;
+  const long long warps = (long long)T * (Hq + (v_in ? 2 : 1) * Hkv);
+  const int blocks = (int)std::min<long long>((warps + 7) / 8, (long long)ds->num_sms * 16);
+  qk_norm_rope_store_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("qk_norm_rope_store_kernel");
+}
+
+int b200_store_kvcache(const void* key, long long key_stride, const void* value,
+                       long long value_stride, void* k_cache, void* v_cache,
+                       const int* slot_mapping, int T, int D, long long num_slots,
+                       b200_stream_t stream) {
+  if (T <= 0) return B200_OK;
+  if (D <= 0 || D % 8 || key_stride % 8 || value_stride % 8 || !aligned16(key) ||
+      !aligned16(value) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(B200_ERR_INVALID, "store_kvcache: D and strides must be multiples of 8 elements, 16-byte aligned");
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  const long long vecs = (long long)T * (D / 8);
+  const int blocks = (int)std::min<long long>((vecs + 255) / 256, (long long)ds->num_sms * 8);
+  store_kvcache_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(key), key_stride, static_cast<const __nv_bfloat16*>(value),
+      value_stride, static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
+      slot_mapping, T, D, num_slots, ds->err);
+  return check_launch("store_kvcache_kernel");
+}
+
+int b200_silu_and_mul(const void* x, long long x_stride, void* out, long long out_stride, int T,
+                      int I, b200_stream_t stream) {
+  if (T <= 0) return B200_OK;
+  if (I <= 0 || I % 8 || x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(out))
+    return fail(B200_ERR_INVALID, "silu_and_mul: I and strides must be multiples of 8");
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  const long long vecs = (long long)T * (I / 8);
+  const int blocks = (int)std::min<long long>((vecs + 255) / 256, (long long)ds->num_sms * 8);
+  silu_and_mul_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), x_stride, static_cast<__nv_bfloat16*>(out), out_stride,
+      T, I);
+  return check_launch("silu_and_mul_kernel");
+}
+
+int b200_embedding(const long long* ids, const void* weight, void* out, int T, int H,
+                   long long vocab_start, long long vocab_end, b200_stream_t stream) {
+  if (T <= 0) return B200_OK;
+  if (H <= 0 || H % 8 || !aligned16(weight) || !aligned16(out))
+    return fail(B200_ERR_INVALID, "embedding: H must be a multiple of 8");
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  const long long vecs = (long long)T * (H / 8);
+  const int blocks = (int)std::min<long long>((vecs + 255) / 256, (long long)ds->num_sms * 8);
+  embedding_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      ids, static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out), T, H,
+      vocab_start, vocab_end, ds->err);
+  return check_launch("embedding_kernel");
+}
+
+int b200_argmax(const void* logits, long long stride, int rows, int V, long long* out,
+                b200_stream_t stream) {
+  if (rows <= 0) return B200_OK;
+  if (V <= 0) return fail(B200_ERR_INVALID, "argmax: V must be positive");
+  argmax_kernel<<<rows, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(logits), stride, V, out);
+  return check_launch("argmax_kernel");
+}
+
+int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_t* bytes) {
+  if (!bytes || max_seqs < 0 || max_seqlen_k < 0 || Hq <= 0)
+    return fail(B200_ERR_INVALID, "bad arguments");
+  const size_t chunks = (size_t)max_seqs * ((max_seqlen_k + kDecChunk - 1) / kDecChunk);
+  const size_t head = ((size_t)(max_seqs + 1) * sizeof(int) + 255) / 256 * 256;
+  *bytes = head + chunks * Hq * (kHD + 2) * sizeof(float);
+  return B200_OK;
+}
+
+int b200_paged_attention(const void* q, long long q_stride, const void* k, long long k_stride,
+                         const void* v, long long v_stride, const void* k_cache,
+                         const void* v_cache, long long num_slots, const int* block_tables,
+                         int bt_stride, int bt_width, const int* cu_seqlens_q, const int* cu_seqlens_k, int B,
+                         int max_seqlen_q, int max_seqlen_k, int Hq, int Hkv, int page,
+                         float softmax_scale, void* out, long long out_stride, void* workspace,
+                         size_t ws_bytes, b200_stream_t stream) {
+  if (B <= 0 || max_seqlen_q <= 0) return B200_OK;
+  if (Hq <= 0 || Hkv <= 0 || Hq % Hkv) return fail(B200_ERR_INVALID, "attention: Hq %% Hkv != 0");
+  if (q_stride % 8 || out_stride % 8 || !aligned16(q) || !aligned16(out))
+    return fail(B200_ERR_INVALID, "attention: q/out rows must be 16-byte aligned");
+  if (block_tables && (!k_cache || !v_cache || page <= 0 || !aligned16(k_cache) || !aligned16(v_cache)))
+    return fail(B200_ERR_INVALID, "attention: block tables need an aligned cache and page > 0");
+  if (!block_tables && (!k || !v || k_stride % 8 || v_stride % 8 || !aligned16(k) || !aligned16(v)))
+    return fail(B200_ERR_INVALID, "attention: contiguous K/V must be 16-byte aligned rows");
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int G = Hq / Hkv;
+  const float scale_log2 = softmax_scale * 1.4426950408889634f;
+  if (max_seqlen_q == 1 && block_tables && G <= 8 && B <= kMaxPlanSeqs) {
+    const size_t head = ((size_t)(B + 1) * sizeof(int) + 255) / 256 * 256;
+    if (!workspace || ws_bytes <= head || !aligned16(workspace))
+      return fail(B200_ERR_WORKSPACE, "attention: decode workspace missing or too small");
+    const size_t per_chunk = (size_t)Hq * (kHD + 2) * sizeof(float);
+    DecodeArgs a{};
+    a.q = static_cast<const __nv_bfloat16*>(q); a.q_stride = q_stride;
+    a.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
+    a.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
+    a.block_tables = block_tables; a.bt_stride = bt_stride; a.bt_width = bt_width;
+    a.cu_q = cu_seqlens_q; a.cu_k = cu_seqlens_k;
+    a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = G; a.page = page; a.num_slots = num_slots;
+    a.scale_log2 = scale_log2;
+    a.cap_chunks = (long long)((ws_bytes - head) / per_chunk);
+    a.chunk_start = static_cast<int*>(workspace);
+    a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + head);
+    a.part_o = a.part_ml + (size_t)a.cap_chunks * Hq * 2;
+    a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
+    a.err = ds->err;
+    const int smem = 65536 + ((B + 1) + 8) * (int)sizeof(int);
+    if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
+    const long long bound = (long long)B * ((max_seqlen_k + kDecChunk - 1) / kDecChunk) * Hkv;
+    const int blocks = (int)std::max(1LL, std::min<long long>(bound, (long long)ds->num_sms * 3));
+    decode_attn_kernel<<<blocks, 128, smem, st>>>(a);
+    if (int r = check_launch("decode_attn_kernel")) return r;
+    decode_combine_kernel<<<dim3(B, Hq), 128, 0, st>>>(a);
+    return check_launch("decode_combine_kernel");
+  }
+  PrefillArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q); a.q_stride = q_stride;
+  a.k = static_cast<const __nv_bfloat16*>(k); a.v = static_cast<const __nv_bfloat16*>(v);
+  a.k_stride = k_stride; a.v_stride = v_stride;
+  a.k_cache = block_tables ? static_cast<const __nv_bfloat16*>(k_cache) : nullptr;
+  a.v_cache = block_tables ? static_cast<const __nv_bfloat16*>(v_cache) : nullptr;
+  a.block_tables = block_tables; a.bt_stride = bt_stride; a.bt_width = bt_width; a.num_slots = num_slots;
+  a.cu_q = cu_seqlens_q; a.cu_k = cu_seqlens_k;
+  a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = G; a.page = page;
+  a.scale_log2 = scale_log2;
+  a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
+  a.err = ds->err;
+  const int smem = 16384 + 2 * 32768;
+  if (int r = ensure_smem(ds, 4u, prefill_attn_kernel, smem)) return r;
+  dim3 grid((max_seqlen_q + kPfBM - 1) / kPfBM, Hq, B);
+  prefill_attn_kernel<<<grid, 128, smem, st>>>(a);
+  return check_launch("prefill_attn_kernel");
+}
+
+}  // extern "C"
