@@ -1,0 +1,503 @@
+"""Decode throughput of the B200 Qwen3 decoder path (one JSON line on rank 0).
+
+Workload ("qwen3-8b-decode-mix256"): Qwen3-8B architecture, random-init bf16
+weights N(0, 0.02), tensor parallel over the N GPUs (TP = N, strong scaling:
+the same 256-sequence batch at every N).  The 256 sequences are the
+synthetic serving mix: prompt ~U[100, 1024] tokens, output budget
+~U[100, 1024], captured mid-generation (generated ~U[1, budget]), so a decode
+step attends over ~843 cached tokens per sequence on average.  The paged KV
+cache (block 256, random permutation of physical blocks) holds synthetic
+N(0, 1) keys/values.
+
+One step = one greedy decode step for all 256 sequences: embedding, 36
+decoder layers (qkv GEMM, q/k norm + RoPE + KV write, paged attention,
+o_proj, RMSNorm, gate_up + SiLU, down_proj), final norm, LM head, argmax --
+replayed from one CUDA graph.  Each step feeds back its argmax tokens and
+advances every position by one.
+
+  value : tok/s with the step metadata already resident in HBM (device-timed
+          CUDA events around K steps, max over ranks)
+  e2e   : tok/s through the runner's public API with host buffers: metadata
+          built on the host, pinned H2D copies, graph replay, tokens copied
+          back (D2H) every step
+  roofline : the dominant kernel (paged decode attention) timed live with
+          CUDA events over its standalone launch on one layer's inputs
+
+`--impl reference` times the oracle (a CPU port of the reference's torch
+path) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "nano-vllm-diy_b200")
+for p in (REPO, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "decode tok/s, Qwen3-8B bf16, TP 1/2/4/8"
+UNIT = "tok/s"
+WORKLOAD = "qwen3-8b-decode-mix256"
+BLOCK = 256
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def mix(batch: int, seed: int):
+    """Context length (cached tokens + the new one) of each sequence."""
+    rng = random.Random(seed)
+    lens = []
+    for _ in range(batch):
+        prompt = rng.randint(100, 1024)
+        budget = rng.randint(100, 1024)
+        gen = rng.randint(1, budget)
+        lens.append(prompt + gen)
+    return lens
+
+
+def qwen3_8b_config():
+    from oracle.weights import QWEN3_8B
+    import dataclasses
+    return dataclasses.replace(QWEN3_8B, max_pos=4096)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        try:
+            self.gpu = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.gpu = str(device.index)
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        under = [s for s in sm if s > 0.5 * max(sm)] if sm else []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(under) if under else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# CPU side: the oracle port of the reference path
+# --------------------------------------------------------------------------
+class CpuDecodeSample:
+    """The oracle (the reference's torch path restated for the CPU) on the host
+    cores: one Qwen3-8B decoder layer over `n_seqs` decode sequences of the
+    mix, plus the LM head for those tokens.  GEMMs use torch's bf16 F.linear,
+    the op the reference calls.  tok/s = n_seqs / (36 x layer time + head
+    time): an extrapolation from one layer, stated in the sample text."""
+
+    def __init__(self, n_seqs: int = 8, seed: int = 0):
+        from oracle import layers as L
+        from oracle import model as OM
+        from oracle.weights import random_weights
+        import dataclasses
+        torch.set_num_threads(os.cpu_count() or 1)
+        L.NATIVE_BF16_LINEAR = True
+        self.L, self.OM = L, OM
+        self.full = qwen3_8b_config()
+        self.one = dataclasses.replace(self.full, layers=1)
+        # random weights for the layer; the 151936-row embedding / LM head are a
+        # small random block tiled to full size (their values do not change
+        # the CPU time, and drawing 1.2 G normals would dominate the setup)
+        self.W = random_weights(dataclasses.replace(self.one, vocab=4096), seed=seed)
+        for name in ("model.embed_tokens.weight", "lm_head.weight"):
+            small = self.W[name]
+            reps = (self.full.vocab + small.shape[0] - 1) // small.shape[0]
+            self.W[name] = small.repeat(reps, 1)[:self.full.vocab].contiguous()
+        self.n = n_seqs
+        self.lens = mix(256, seed)[:n_seqs]
+        nblk = sum((n + BLOCK - 1) // BLOCK for n in self.lens)
+        self.kv = OM.OracleKV(self.one, nblk, BLOCK)
+        g = torch.Generator().manual_seed(seed)
+        self.kv.k[0].copy_(torch.randn(self.kv.k[0].shape, generator=g).to(torch.bfloat16))
+        self.kv.v[0].copy_(torch.randn(self.kv.v[0].shape, generator=g).to(torch.bfloat16))
+        bt = torch.full((n_seqs, max((n + BLOCK - 1) // BLOCK for n in self.lens)), -1,
+                        dtype=torch.int32)
+        nxt = 0
+        for i, n in enumerate(self.lens):
+            for j in range((n + BLOCK - 1) // BLOCK):
+                bt[i, j] = nxt
+                nxt += 1
+        self.pos = torch.tensor([n - 1 for n in self.lens], dtype=torch.int64)
+        slots = torch.tensor([int(bt[i, (n - 1) // BLOCK]) * BLOCK + (n - 1) % BLOCK
+                              for i, n in enumerate(self.lens)], dtype=torch.int32)
+        self.ctx = dict(cu_seqlens_q=torch.arange(n_seqs + 1, dtype=torch.int32),
+                        cu_seqlens_k=torch.tensor([0] + list(np.cumsum(self.lens)), dtype=torch.int32),
+                        slot_mapping=slots, block_tables=bt, is_prefill=False)
+        self.ids = torch.randint(0, 10000, (n_seqs,), generator=g)
+        self.cos_sin = L.rope_cos_sin(self.one.max_pos, self.one.head_dim, self.one.theta)
+        h = self.layer()
+        a = time.perf_counter()
+        OM.compute_logits(self.one, self.W, h, self.ctx)
+        self.t_head = time.perf_counter() - a
+
+    def layer(self):
+        return self.OM.forward(self.one, self.W, self.ids, self.pos, self.ctx, self.kv,
+                               cos_sin=self.cos_sin)
+
+    def time_layer(self) -> float:
+        a = time.perf_counter()
+        self.layer()
+        return time.perf_counter() - a
+
+    def tok_per_s(self, t_layer: float) -> float:
+        return self.n / (t_layer * self.full.layers + self.t_head)
+
+    def describe(self, reps: int) -> dict:
+        return {"unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                "sample": (f"oracle torch-CPU port (bf16 F.linear as the reference): {reps} x one "
+                           f"Qwen3-8B decoder layer over {self.n} decode sequences of the mix "
+                           f"(mean ctx {np.mean(self.lens):.0f}) + LM head; tok/s extrapolated "
+                           f"to 36 layers")}
+
+
+def cpu_baseline(seconds: float, seed: int) -> dict:
+    smp = CpuDecodeSample(n_seqs=8, seed=seed)
+    times = []
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds or not times:
+        times.append(smp.time_layer())
+    d = smp.describe(len(times))
+    d["value"] = smp.tok_per_s(float(np.median(times)))
+    return d
+
+
+def run_reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return
+    smp = CpuDecodeSample(n_seqs=8, seed=args.seed)
+    for _ in range(args.warmup):
+        smp.time_layer()
+    times = [smp.time_layer() for _ in range(args.steps)]
+    value = smp.tok_per_s(float(np.mean(times)))
+    d = smp.describe(len(times))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * 256 / value, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": 256, "tp": 1, "device": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": d["cores"], "kind": "port",
+                         "sample": d["sample"]},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU side
+# --------------------------------------------------------------------------
+@torch.inference_mode()
+def run_b200(args, rank: int, world: int):
+    import torch.distributed as dist
+    from src import b200
+    from src.engine.model_runner import ModelRunner
+    from src.layers import tp_comm
+
+    torch.cuda.set_device(rank % torch.cuda.device_count())
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=__import__("datetime").timedelta(seconds=120))
+        if args.fused_ar:
+            try:
+                from src.layers import tp_allreduce
+            except ImportError:
+                args.fused_ar = False
+            else:
+                tp_comm.set_comm(tp_allreduce.FusedRowParallel.create(dev))
+    shape = qwen3_8b_config()
+    cfg = shape.hf_config()
+    B = args.batch
+    lens = mix(B, args.seed)
+    steps_total = args.warmup + args.steps + 2
+    max_len = max(lens) + steps_total
+    runner = ModelRunner(cfg, rank=rank, world_size=world, block_size=BLOCK, max_num_seqs=B,
+                         max_seq_len=max(4096, max_len), device=dev)
+    runner.init_random_weights(seed=args.seed)
+    per_seq = [(n + steps_total + BLOCK - 1) // BLOCK for n in lens]
+    nblk = sum(per_seq) + 4
+    runner.allocate_kv_cache(nblk)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    for i in range(runner.kv_cache.shape[0]):
+        for j in range(runner.kv_cache.shape[1]):
+            runner.kv_cache[i, j].normal_(0.0, 1.0, generator=g)
+    perm = np.random.default_rng(args.seed).permutation(nblk)
+    width = max(per_seq)
+    bt = np.full((B, width), -1, dtype=np.int32)
+    k = 0
+    for i, n in enumerate(per_seq):
+        bt[i, :n] = perm[k:k + n]
+        k += n
+
+    launches0 = b200.launch_count()
+    runner.capture_cudagraph([B], with_sampling=True)
+    kernels_per_step = b200.launch_count() - launches0  # warm-up + capture launch the same set
+    kernels_per_step //= 2
+    v = runner.graph_vars
+
+    # device-resident metadata for every step
+    S = steps_total
+    lens_t = torch.tensor(lens, dtype=torch.int64)
+    pos_all = torch.stack([lens_t - 1 + s for s in range(S)])                     # [S, B]
+    bt_t = torch.from_numpy(bt).long()
+    slot_all = (bt_t.gather(1, pos_all.t() // BLOCK).t() * BLOCK + pos_all % BLOCK).to(torch.int32)
+    cuk_all = torch.zeros(S, B + 1, dtype=torch.int32)
+    cuk_all[:, 1:] = torch.cumsum(pos_all + 1, dim=1).to(torch.int32)
+    pos_d, slot_d, cuk_d = pos_all.to(dev), slot_all.to(dev), cuk_all.to(dev)
+    v["cu_seqlens_q"][:B + 1] = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    v["block_tables"][:B, :width] = torch.from_numpy(bt).to(dev)
+    v["tokens"][:B] = torch.randint(0, 10000, (B,), device=dev, generator=g)
+
+    def device_step(s):
+        v["input_ids"][:B].copy_(v["tokens"][:B])
+        v["positions"][:B].copy_(pos_d[s])
+        v["slot_mapping"][:B].copy_(slot_d[s])
+        v["cu_seqlens_k"][:B + 1].copy_(cuk_d[s])
+        runner.replay(B)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    stream = torch.cuda.current_stream()
+    for s in range(args.warmup):
+        device_step(s)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        ev0.record(stream)
+        for s in range(args.warmup, args.warmup + args.steps):
+            device_step(s)
+        ev1.record(stream)
+        barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    value = B / (ms / 1000.0)
+    clock_summary = clocks.summary()
+
+    # ---- e2e: host metadata -> pinned H2D -> replay -> D2H tokens, per step
+    h_lens = np.asarray(lens, dtype=np.int64)
+    pin = {
+        "ids": torch.empty(B, dtype=torch.int64).pin_memory(),
+        "pos": torch.empty(B, dtype=torch.int64).pin_memory(),
+        "slot": torch.empty(B, dtype=torch.int32).pin_memory(),
+        "cuq": torch.empty(B + 1, dtype=torch.int32).pin_memory(),
+        "cuk": torch.empty(B + 1, dtype=torch.int32).pin_memory(),
+        "bt": torch.from_numpy(bt).pin_memory(),
+        "tok": torch.empty(B, dtype=torch.int64).pin_memory(),
+    }
+    h2d = sum(pin[k].numel() * pin[k].element_size() for k in ("ids", "pos", "slot", "cuq", "cuk", "bt"))
+    d2h = pin["tok"].numel() * pin["tok"].element_size()
+    tokens_host = np.random.default_rng(args.seed).integers(0, 10000, B)
+
+    def e2e_step(s):
+        pos = h_lens - 1 + s
+        pin["ids"].numpy()[:] = tokens_host
+        pin["pos"].numpy()[:] = pos
+        pin["slot"].numpy()[:] = bt[np.arange(B), pos // BLOCK] * BLOCK + pos % BLOCK
+        pin["cuq"].numpy()[:] = np.arange(B + 1)
+        pin["cuk"].numpy()[0] = 0
+        np.cumsum(pos + 1, out=pin["cuk"].numpy()[1:])
+        v["input_ids"][:B].copy_(pin["ids"], non_blocking=True)
+        v["positions"][:B].copy_(pin["pos"], non_blocking=True)
+        v["slot_mapping"][:B].copy_(pin["slot"], non_blocking=True)
+        v["cu_seqlens_q"][:B + 1].copy_(pin["cuq"], non_blocking=True)
+        v["cu_seqlens_k"][:B + 1].copy_(pin["cuk"], non_blocking=True)
+        v["block_tables"][:B, :width].copy_(pin["bt"], non_blocking=True)
+        runner.replay(B)
+        pin["tok"].copy_(v["tokens"][:B], non_blocking=True)
+        stream.synchronize()
+        tokens_host[:] = pin["tok"].numpy()
+
+    for s in range(args.warmup):
+        e2e_step(s)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(args.warmup, args.warmup + args.steps):
+        e2e_step(s)
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    # ---- roofline: decode attention of one layer, timed standalone
+    hbm_peak, _, peak_kind = peaks()
+    from src.layers.attention import attend
+    from src.utils.context import Context
+    attn_mod = runner.model.model.layers[0].self_attn
+    s_last = args.warmup + args.steps - 1
+    ctx = Context(is_prefill=False, cu_seqlens_q=v["cu_seqlens_q"][:B + 1].clone(),
+                  cu_seqlens_k=cuk_d[s_last].clone(), max_seqlen_q=1,
+                  max_seqlen_k=runner.max_seq_len, slot_mapping=slot_d[s_last].clone(),
+                  block_tables=v["block_tables"][:B].clone())
+    Hq = runner.local_q_heads
+    q = torch.randn(B, Hq, 128, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    with torch.inference_mode():
+        for _ in range(3):
+            attend(q, None, None, attn_mod.attn.k_cache, attn_mod.attn.v_cache, ctx, attn_mod.scaling, out=out)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        a0.record(stream)
+        for _ in range(reps):
+            attend(q, None, None, attn_mod.attn.k_cache, attn_mod.attn.v_cache, ctx, attn_mod.scaling, out=out)
+        a1.record(stream)
+        torch.cuda.synchronize()
+    attn_ms = a0.elapsed_time(a1) / reps
+    ctx_sum = int((pos_all[s_last] + 1).sum())
+    kv_bytes = ctx_sum * runner.local_kv_heads * 128 * 2 * 2
+    qo_bytes = 2 * B * Hq * 128 * 2
+    attn_bytes = kv_bytes + qo_bytes
+    achieved = attn_bytes / (attn_ms / 1000.0) / 1e9
+    # whole-step bytes: weights + KV read + KV write of the new tokens
+    w_bytes = sum(p.numel() * p.element_size() for n, p in runner.model.named_parameters()
+                  if "embed_tokens" not in n)
+    step_bytes = w_bytes + kv_bytes * shape.layers + B * runner.local_kv_heads * 128 * 4 * shape.layers
+    step_gbs = step_bytes / (ms / 1000.0) / 1e9
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "decode_attention_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as f:
+                tr = json.load(f)
+            # captured on a smaller case: scale by the KV bytes processed
+            traffic = tr["dram_bytes"] * attn_bytes / tr["algorithmic_bytes"]
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        cpu = cpu_baseline(args.cpu_seconds, args.seed)
+
+    if world > 1:
+        tp_comm.clear()
+    runner.release_graphs()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) KV, seeded mix)",
+            "config": {"workload": WORKLOAD, "batch": B, "tp": world, "parallelism": f"tp{world}",
+                       "mean_ctx": float(np.mean(lens)), "block_size": BLOCK,
+                       "l2": "inputs larger than L2 (16.4 GB weights + KV per step)",
+                       "fused_allreduce": bool(world > 1 and args.fused_ar)},
+            "roofline": {"bound": "hbm", "kernel": "decode_attn_kernel+decode_combine_kernel",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_source": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes": attn_bytes,
+                         "launch_ms": attn_ms},
+            "step_roofline": {"bytes": step_bytes, "achieved_gbs": step_gbs,
+                              "frac": step_gbs / hbm_peak},
+            "cpu_baseline": cpu,
+            "e2e": {"value": B / (e2e_ms / 1000.0), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": kernels_per_step * args.steps,
+            "clocks": clock_summary,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-fused-ar", dest="fused_ar", action="store_false")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    run_b200(args, rank, world)
+
+
+if __name__ == "__main__":
+    main()

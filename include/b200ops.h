@@ -45,6 +45,10 @@ typedef struct CUstream_st* b200_stream_t; /* == cudaStream_t */
 const char* b200_last_error(void);
 int b200_version(void);
 
+/* Kernels launched by this library from the host so far (a CUDA-graph
+ * capture counts each captured launch once; replays are not counted). */
+unsigned long long b200_launch_count(void);
+
 /* Reads the device error word of the current device; clears it when `clear`
  * is non-zero.  Synchronous. */
 int b200_device_error(unsigned* out, int clear);

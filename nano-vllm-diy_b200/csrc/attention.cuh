@@ -216,15 +216,24 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
     mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
     mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
     float lsum = 0.f;
-    uint32_t pa[2][4];
+    // P enters the PV MMA as bf16 hi + lo parts: hi = bf16(p), lo = bf16(p - hi),
+    // so the product keeps ~16 mantissa bits of p instead of 8.
+    uint32_t pa[2][4], pl[2][4];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       const float p0 = mloc == -INFINITY ? 0.f : fast_exp2(s[nt][0] - mloc);
       const float p1 = mloc == -INFINITY ? 0.f : fast_exp2(s[nt][1] - mloc);
       lsum += p0 + p1;
       const uint32_t pk = pack_bf16x2(p0, p1);
-      if ((nt & 1) == 0) { pa[nt >> 1][0] = pk; pa[nt >> 1][1] = 0u; }
-      else { pa[nt >> 1][2] = pk; pa[nt >> 1][3] = 0u; }
+      const float2 ph = unpack_bf16x2(pk);
+      const uint32_t lk = pack_bf16x2(p0 - ph.x, p1 - ph.y);
+      if ((nt & 1) == 0) {
+        pa[nt >> 1][0] = pk; pa[nt >> 1][1] = 0u;
+        pl[nt >> 1][0] = lk; pl[nt >> 1][1] = 0u;
+      } else {
+        pa[nt >> 1][2] = pk; pa[nt >> 1][3] = 0u;
+        pl[nt >> 1][2] = lk; pl[nt >> 1][3] = 0u;
+      }
     }
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
@@ -247,6 +256,8 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
           ldmatrix_x4_trans(sVw + swz(r, 2 * dp + (mi >> 1)), v0, v1, v2, v3);
           mma_bf16_16816(o[2 * dp], pa[kp], v0, v1);
           mma_bf16_16816(o[2 * dp + 1], pa[kp], v2, v3);
+          mma_bf16_16816(o[2 * dp], pl[kp], v0, v1);
+          mma_bf16_16816(o[2 * dp + 1], pl[kp], v2, v3);
         }
       }
     }
@@ -461,7 +472,7 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
       m_r[rr] = mnew;
     }
     float ls[2] = {0.f, 0.f};
-    uint32_t pa[4][4];
+    uint32_t pa[4][4], pl[4][4];  // bf16 hi / lo parts of P (see decode kernel)
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       float p[4];
@@ -471,13 +482,18 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
         p[e] = (mm == -INFINITY) ? 0.f : fast_exp2(s[nt][e] - mm);
         ls[e >> 1] += p[e];
       }
+      const uint32_t h01 = pack_bf16x2(p[0], p[1]);
+      const uint32_t h23 = pack_bf16x2(p[2], p[3]);
+      const float2 f01 = unpack_bf16x2(h01), f23 = unpack_bf16x2(h23);
+      const uint32_t l01 = pack_bf16x2(p[0] - f01.x, p[1] - f01.y);
+      const uint32_t l23 = pack_bf16x2(p[2] - f23.x, p[3] - f23.y);
       const int kp = nt >> 1;
       if ((nt & 1) == 0) {
-        pa[kp][0] = pack_bf16x2(p[0], p[1]);
-        pa[kp][1] = pack_bf16x2(p[2], p[3]);
+        pa[kp][0] = h01; pa[kp][1] = h23;
+        pl[kp][0] = l01; pl[kp][1] = l23;
       } else {
-        pa[kp][2] = pack_bf16x2(p[0], p[1]);
-        pa[kp][3] = pack_bf16x2(p[2], p[3]);
+        pa[kp][2] = h01; pa[kp][3] = h23;
+        pl[kp][2] = l01; pl[kp][3] = l23;
       }
     }
 #pragma unroll
@@ -500,6 +516,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) 
         ldmatrix_x4_trans(sVs + swz(r, 2 * dp + (mi >> 1)), v0, v1, v2, v3);
         mma_bf16_16816(o[2 * dp], pa[kp], v0, v1);
         mma_bf16_16816(o[2 * dp + 1], pa[kp], v2, v3);
+        mma_bf16_16816(o[2 * dp], pl[kp], v0, v1);
+        mma_bf16_16816(o[2 * dp + 1], pl[kp], v2, v3);
       }
     }
     __syncthreads();  // stage (t & 1) is refilled two iterations later

@@ -37,7 +37,12 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// Number of kernels this library has launched from the host (graph replays
+// launch without the host and are not counted).
+unsigned long long g_launches = 0;
+
 int check_launch(const char* what) {
+  ++g_launches;
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return B200_OK;
@@ -225,6 +230,8 @@ extern "C" {
 const char* b200_last_error(void) { return g_last_error.c_str(); }
 
 int b200_version(void) { return B200_ABI_VERSION; }
+
+unsigned long long b200_launch_count(void) { return g_launches; }
 
 int b200_device_error(unsigned* out, int clear) {
   DeviceState* ds;

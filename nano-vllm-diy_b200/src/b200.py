@@ -31,6 +31,7 @@ _sz = ctypes.c_size_t
 _SIGNATURES = {
     "b200_last_error": ([], ctypes.c_char_p),
     "b200_version": ([], _i),
+    "b200_launch_count": ([], ctypes.c_ulonglong),
     "b200_device_error": ([ctypes.POINTER(ctypes.c_uint), _i], _i),
     "b200_linear_workspace_bytes": ([_i, _i, _i, ctypes.POINTER(_sz)], _i),
     "b200_linear": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _c_void_p, _ll, _i, _i, _i,
@@ -140,6 +141,11 @@ def reserve_workspace(kind: str, nbytes: int, device: torch.device) -> None:
 
 
 GEMM_WS_DEFAULT = 64 << 20
+
+
+def launch_count() -> int:
+    """Kernels launched by libb200ops from the host so far."""
+    return int(load_library().b200_launch_count())
 
 
 def device_error(clear: bool = True) -> int:

@@ -12,10 +12,16 @@ import torch
 
 BF16 = torch.bfloat16
 
+# When True, linear() calls torch's bf16 F.linear -- the op the reference
+# itself calls -- instead of the fp32 restatement (used for CPU timing only).
+NATIVE_BF16_LINEAR = False
+
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
     """F.linear in bf16: fp32 accumulation, one rounding of the output.
     src/layers/linear.py:74-75, :169-170; src/layers/llm_head.py:64."""
+    if NATIVE_BF16_LINEAR:
+        return torch.nn.functional.linear(x, w, bias)
     y = x.float() @ w.float().t()
     if bias is not None:
         y = y + bias.float()
