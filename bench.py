@@ -477,6 +477,88 @@ def run_b200(args, rank: int, world: int):
         dist.destroy_process_group()
 
 
+def run_microbench(args):
+    """Kernel microbenchmarks (one JSON line each), used for ncu captures.
+      attn : BASELINE config 3 -- paged decode attention, B=256, ctx ~U[128,4096],
+             32 q / 8 kv heads, N(0,1) bf16, block 256, random block permutation,
+             seed 1 -- plus the slot_mapping scatter of 256 new tokens
+      gemm : the Qwen3-8B TP1 decode GEMMs at 256 tokens"""
+    from src import b200
+    from src.layers.attention import attend
+    from src.utils.context import Context
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, tflops, kind = peaks()
+    reps = args.steps
+
+    def timeit(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    with torch.inference_mode():
+        if args.workload == "attn":
+            g = torch.Generator().manual_seed(1)
+            B, Hq, Hkv = 256, 32, 8
+            lens = torch.randint(128, 4097, (B,), generator=g)
+            pages = (lens + BLOCK - 1) // BLOCK
+            nblk = int(pages.sum()) + 1
+            perm = torch.randperm(nblk, generator=g)
+            width = int(pages.max())
+            bt = torch.full((B, width), -1, dtype=torch.int32)
+            k = 0
+            for i, n in enumerate(pages.tolist()):
+                bt[i, :n] = perm[k:k + n].to(torch.int32)
+                k += n
+            gd = torch.Generator(device=dev).manual_seed(1)
+            kc = torch.randn(nblk, BLOCK, Hkv, 128, generator=gd, device=dev).to(torch.bfloat16)
+            vc = torch.randn(nblk, BLOCK, Hkv, 128, generator=gd, device=dev).to(torch.bfloat16)
+            q = torch.randn(B, Hq, 128, generator=gd, device=dev).to(torch.bfloat16)
+            cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
+            cu_k = torch.zeros(B + 1, dtype=torch.int32)
+            cu_k[1:] = torch.cumsum(lens, 0)
+            ctx = Context(is_prefill=False, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k.to(dev),
+                          max_seqlen_q=1, max_seqlen_k=4096, block_tables=bt.to(dev))
+            out = torch.empty_like(q)
+            ms = timeit(lambda: attend(q, None, None, kc, vc, ctx, 128 ** -0.5, out=out))
+            byts = int(lens.sum()) * Hkv * 128 * 2 * 2 + 2 * B * Hq * 128 * 2
+            # the scatter of 256 new tokens into their slots
+            pos = lens - 1
+            slots = (bt.long().gather(1, (pos // BLOCK)[:, None])[:, 0] * BLOCK + pos % BLOCK).to(torch.int32).to(dev)
+            knew = torch.randn(B, Hkv, 128, generator=gd, device=dev).to(torch.bfloat16)
+            ms_sc = timeit(lambda: b200.store_kvcache(knew, knew, kc, vc, slots))
+            sc_bytes = 2 * B * Hkv * 128 * 2 * 2
+            print(json.dumps({"workload": "attn-microbench (config 3)", "decode_attn_ms": ms,
+                              "bytes": byts, "gbs": byts / ms / 1e6, "frac": byts / ms / 1e6 / hbm,
+                              "scatter_ms": ms_sc, "scatter_gbs": sc_bytes / ms_sc / 1e6,
+                              "peak_gbs": hbm, "peak_source": kind}), flush=True)
+        else:
+            T = 256
+            shapes = {"qkv": (6144, 4096), "o_proj": (4096, 4096), "gate_up": (24576, 4096),
+                      "down": (4096, 12288), "lm_head": (151936, 4096)}
+            res = {}
+            for name, (N, K) in shapes.items():
+                x = torch.randn(T, K, device=dev).to(torch.bfloat16)
+                w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+                if name == "gate_up":
+                    fn = lambda: b200.linear_silu_and_mul(x, w)
+                else:
+                    fn = lambda: b200.linear(x, w)
+                ms = timeit(fn)
+                byts = N * K * 2 + T * K * 2 + T * (N // 2 if name == "gate_up" else N) * 2
+                res[name] = {"ms": ms, "gbs": byts / ms / 1e6, "frac": byts / ms / 1e6 / hbm}
+                del x, w
+            print(json.dumps({"workload": "gemm-microbench (Qwen3-8B TP1 decode, T=256)",
+                              "kernels": res, "peak_gbs": hbm}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -488,6 +570,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-fused-ar", dest="fused_ar", action="store_false")
+    ap.add_argument("--workload", default="decode", choices=["decode", "attn", "gemm"],
+                    help="decode = the headline line; attn / gemm = kernel microbenchmarks")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -495,6 +579,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.workload != "decode":
+        run_microbench(args)
         return
     run_b200(args, rank, world)
 

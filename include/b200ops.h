@@ -150,9 +150,12 @@ int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_
  *    block_tables == NULL: K/V from contiguous k / v rows cu_seqlens_k[b]+j.
  *  - cu_seqlens_q / cu_seqlens_k: int32 [B + 1] on the device; sequences
  *    with q length <= 0 (CUDA-graph padding) are skipped.
- *  - max_seqlen_q == 1 with a block table takes the split-KV decode kernel
- *    and needs `workspace` (b200_attention_workspace_bytes); max_seqlen_k
- *    only bounds the launch. */
+ *  - max_seqlen_q == 1 with a block table (B <= 1024, Hkv <= 64, Hq/Hkv <= 8,
+ *    page a multiple of 256) takes the split-KV decode kernel and needs
+ *    `workspace` (b200_attention_workspace_bytes).  Its first 256 KiB hold
+ *    per-(sequence, kv head) tickets that must be zero before the first call
+ *    and are zero again after every call; the rest is per-call scratch.
+ *    Calls that share a workspace must not overlap on the GPU. */
 int b200_paged_attention(const void* q, long long q_stride, const void* k, long long k_stride,
                          const void* v, long long v_stride, const void* k_cache,
                          const void* v_cache, long long num_slots, const int* block_tables,

@@ -12,312 +12,22 @@
 //   * lengths are read on the device from cu_seqlens_*; a sequence whose
 //     query length is <= 0 (CUDA-graph padding) is skipped.
 //
-// Two kernels:
-//   decode_attn_kernel   q_len == 1 for every live sequence.  Work item =
-//       (128-token chunk of one sequence, kv head); the G = Hq/Hkv query heads
-//       that share the kv head are the rows of one m16n8k16 MMA, so K/V bytes
-//       are read from HBM exactly once.  A persistent grid walks a device-side
-//       prefix sum of chunks, so the launch shape does not depend on the
-//       context lengths (CUDA-graph safe).  Per-chunk partial (m, l, o) go to
-//       a workspace and decode_combine_kernel merges them.
-//   prefill_attn_kernel  FA2-style: 64 queries x 1 head per CTA, K/V tiles of
-//       64 keys double-buffered with cp.async, online softmax in registers.
+// This file holds prefill_attn_kernel (prefill, chunked prefill, prefix
+// hits and mixed batches): FA2-style, 64 queries x 1 head per CTA, K/V tiles
+// of 64 keys double-buffered with cp.async, online softmax in registers, P
+// fed to the PV MMA as bf16 hi + lo parts.  Pure-decode batches use
+// decode_attention.cuh.
 #pragma once
 #include "common.cuh"
 
 namespace b200 {
 
 constexpr int kHD = 128;          // head_dim
-constexpr int kDecChunk = 128;    // tokens per decode work item
-constexpr int kMaxPlanSeqs = 4095;
-
-struct DecodeArgs {
-  const __nv_bfloat16* q;
-  long long q_stride;  // elements between consecutive tokens of q
-  const __nv_bfloat16* k_cache;
-  const __nv_bfloat16* v_cache;
-  const int* block_tables;
-  int bt_stride;
-  int bt_width;         // valid columns per block-table row
-  const int* cu_q;
-  const int* cu_k;
-  int B, Hq, Hkv, G, page;
-  long long num_slots;  // num_blocks * page
-  float scale_log2;     // softmax_scale * log2(e)
-  float* part_o;        // [cap_chunks][Hq][128]
-  float* part_ml;       // [cap_chunks][Hq][2]
-  long long cap_chunks;
-  int* chunk_start;     // [B + 1], written by CTA 0 for the combine kernel
-  __nv_bfloat16* out;
-  long long out_stride;
-  unsigned* err;
-};
 
 // Swizzled byte offset of 16-byte chunk `ch` of row `r` in a [rows][256 B]
 // tile: chunk index XOR (row % 8) makes every ldmatrix phase conflict-free.
 __device__ __forceinline__ uint32_t swz(int r, int ch) {
   return (uint32_t)(r * 256 + ((ch ^ (r & 7)) << 4));
-}
-
-// Exclusive prefix sum of per-sequence chunk counts into s_start[0..B].
-__device__ __forceinline__ void build_chunk_plan(const DecodeArgs& a, int* s_start, int* s_warp) {
-  const int tid = threadIdx.x;
-  const int per = (a.B + blockDim.x - 1) / blockDim.x;
-  const int beg = min(a.B, tid * per);
-  const int end = min(a.B, beg + per);
-  int local = 0;
-  for (int b = beg; b < end; ++b) {
-    const int nq = a.cu_q[b + 1] - a.cu_q[b];
-    const int nk = a.cu_k[b + 1] - a.cu_k[b];
-    const int cnt = (nq >= 1 && nk > 0) ? (nk + kDecChunk - 1) / kDecChunk : 0;
-    s_start[b] = cnt;  // temporarily the count
-    local += cnt;
-  }
-  // inclusive scan of `local` over the block
-  const int lane = tid & 31, warp = tid >> 5;
-  int incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) s_warp[warp] = incl;
-  __syncthreads();
-  int warp_off = 0;
-  for (int w = 0; w < warp; ++w) warp_off += s_warp[w];
-  int run = warp_off + incl - local;  // exclusive prefix of this thread
-  for (int b = beg; b < end; ++b) {
-    const int cnt = s_start[b];
-    s_start[b] = run;
-    run += cnt;
-  }
-  if (tid == blockDim.x - 1) s_start[a.B] = run;
-  __syncthreads();
-}
-
-__global__ void __launch_bounds__(128) decode_attn_kernel(const DecodeArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* sK = smem;                 // 4 warps x 32 rows x 256 B
-  uint8_t* sV = smem + 32768;
-  int* s_start = reinterpret_cast<int*>(smem + 65536);
-  int* s_warp = s_start + (a.B + 1);
-  float* s_m = reinterpret_cast<float*>(smem);        // merge scratch reuses sK
-  float* s_l = s_m + 32;
-  float* s_o = s_l + 32;                               // [4][8][128]
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  build_chunk_plan(a, s_start, s_warp);
-  if (blockIdx.x == 0)
-    for (int b = tid; b <= a.B; b += blockDim.x) a.chunk_start[b] = s_start[b];
-  const int total = s_start[a.B];
-  if ((long long)total > a.cap_chunks) {
-    if (blockIdx.x == 0 && tid == 0) raise_error(a.err, ERR_BAD_INDEX);
-    return;
-  }
-  const int items = total * a.Hkv;
-  const uint32_t sKw = smem_u32(sK + warp * 8192);
-  const uint32_t sVw = smem_u32(sV + warp * 8192);
-  const int g = lane >> 2;  // MMA row = query head inside the GQA group
-
-  for (int w = blockIdx.x; w < items; w += gridDim.x) {
-    const int c = w / a.Hkv;
-    const int h = w - c * a.Hkv;
-    // sequence owning chunk c: largest b with s_start[b] <= c
-    int lo = 0, hi = a.B - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (s_start[mid] <= c) lo = mid; else hi = mid - 1;
-    }
-    const int b = lo;
-    const int j0 = (c - s_start[b]) * kDecChunk;
-    const int nk = a.cu_k[b + 1] - a.cu_k[b];
-    const int ntok = min(kDecChunk, nk - j0);
-    const int qrow = a.cu_q[b];
-
-    // ---- K then V rows of this warp's 32 tokens -> smem (two cp.async groups)
-    const int* bt = a.block_tables + (size_t)b * a.bt_stride;
-#pragma unroll
-    for (int kv = 0; kv < 2; ++kv) {
-      const __nv_bfloat16* base = kv == 0 ? a.k_cache : a.v_cache;
-      const uint32_t dstw = kv == 0 ? sKw : sVw;
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const int idx = lane + 32 * i;
-        const int r = idx >> 4, ch = idx & 15;
-        const int tok = warp * 32 + r;
-        bool valid = tok < ntok;
-        const __nv_bfloat16* src = base;
-        if (valid) {
-          const int j = j0 + tok;
-          const int col = j / a.page;
-          const long long blk = col < a.bt_width ? bt[col] : -1;
-          const long long slot = blk * a.page + (j % a.page);
-          if (blk < 0 || slot >= a.num_slots) {
-            raise_error(a.err, ERR_BAD_INDEX);
-            valid = false;
-          } else {
-            src = base + ((size_t)slot * a.Hkv + h) * kHD + ch * 8;
-          }
-        }
-        cp_async_16_zfill(dstw + swz(r, ch), src, valid);
-      }
-      cp_async_commit();
-    }
-
-    // ---- Q fragments (rows = heads of the group, rows >= G are zero)
-    uint32_t qa[8][4];
-    {
-      const bool live = g < a.G;
-      const __nv_bfloat16* qp = a.q + (size_t)qrow * a.q_stride + (size_t)(h * a.G + (live ? g : 0)) * kHD;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int d = ks * 16 + 2 * (lane & 3);
-        qa[ks][0] = live ? *reinterpret_cast<const uint32_t*>(qp + d) : 0u;
-        qa[ks][1] = 0u;
-        qa[ks][2] = live ? *reinterpret_cast<const uint32_t*>(qp + d + 8) : 0u;
-        qa[ks][3] = 0u;
-      }
-    }
-
-    cp_async_wait<1>();
-    __syncwarp();
-
-    // ---- S = Q K^T for 32 tokens (4 n-tiles of 8)
-    float s[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-    {
-      const int mi = lane >> 3, rin = lane & 7;
-#pragma unroll
-      for (int kp = 0; kp < 4; ++kp) {
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-          uint32_t b0, b1, b2, b3;
-          const int r = nt * 8 + rin;
-          ldmatrix_x4(sKw + swz(r, 4 * kp + mi), b0, b1, b2, b3);
-          mma_bf16_16816(s[nt], qa[2 * kp], b0, b1);
-          mma_bf16_16816(s[nt], qa[2 * kp + 1], b2, b3);
-        }
-      }
-    }
-
-    // ---- softmax over this warp's tokens (log2 domain)
-    float mloc = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tok = warp * 32 + nt * 8 + 2 * (lane & 3) + e;
-        const float v = tok < ntok ? s[nt][e] * a.scale_log2 : -INFINITY;
-        s[nt][e] = v;
-        mloc = fmaxf(mloc, v);
-      }
-    }
-    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
-    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
-    float lsum = 0.f;
-    // P enters the PV MMA as bf16 hi + lo parts: hi = bf16(p), lo = bf16(p - hi),
-    // so the product keeps ~16 mantissa bits of p instead of 8.
-    uint32_t pa[2][4], pl[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const float p0 = mloc == -INFINITY ? 0.f : fast_exp2(s[nt][0] - mloc);
-      const float p1 = mloc == -INFINITY ? 0.f : fast_exp2(s[nt][1] - mloc);
-      lsum += p0 + p1;
-      const uint32_t pk = pack_bf16x2(p0, p1);
-      const float2 ph = unpack_bf16x2(pk);
-      const uint32_t lk = pack_bf16x2(p0 - ph.x, p1 - ph.y);
-      if ((nt & 1) == 0) {
-        pa[nt >> 1][0] = pk; pa[nt >> 1][1] = 0u;
-        pl[nt >> 1][0] = lk; pl[nt >> 1][1] = 0u;
-      } else {
-        pa[nt >> 1][2] = pk; pa[nt >> 1][3] = 0u;
-        pl[nt >> 1][2] = lk; pl[nt >> 1][3] = 0u;
-      }
-    }
-    lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-    lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-
-    cp_async_wait<0>();
-    __syncwarp();
-
-    // ---- O = P V  (16 dim-tiles of 8)
-    float o[16][4];
-#pragma unroll
-    for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
-    {
-      const int mi = lane >> 3, rin = lane & 7;
-#pragma unroll
-      for (int kp = 0; kp < 2; ++kp) {
-#pragma unroll
-        for (int dp = 0; dp < 8; ++dp) {
-          uint32_t v0, v1, v2, v3;
-          const int r = kp * 16 + 8 * (mi & 1) + rin;
-          ldmatrix_x4_trans(sVw + swz(r, 2 * dp + (mi >> 1)), v0, v1, v2, v3);
-          mma_bf16_16816(o[2 * dp], pa[kp], v0, v1);
-          mma_bf16_16816(o[2 * dp + 1], pa[kp], v2, v3);
-          mma_bf16_16816(o[2 * dp], pl[kp], v0, v1);
-          mma_bf16_16816(o[2 * dp + 1], pl[kp], v2, v3);
-        }
-      }
-    }
-
-    // ---- merge the 4 warps of the CTA, write the chunk partial
-    __syncthreads();  // every warp is done with sK/sV
-    if ((lane & 3) == 0) {
-      s_m[warp * 8 + g] = mloc;
-      s_l[warp * 8 + g] = lsum;
-    }
-#pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      const int d = dt * 8 + 2 * (lane & 3);
-      s_o[(warp * 8 + g) * kHD + d] = o[dt][0];
-      s_o[(warp * 8 + g) * kHD + d + 1] = o[dt][1];
-    }
-    __syncthreads();
-    for (int idx = tid; idx < a.G * kHD; idx += blockDim.x) {
-      const int gg = idx >> 7, d = idx & 127;
-      float M = -INFINITY;
-#pragma unroll
-      for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, s_m[ww * 8 + gg]);
-      float L = 0.f, O = 0.f;
-#pragma unroll
-      for (int ww = 0; ww < 4; ++ww) {
-        const float mw = s_m[ww * 8 + gg];
-        if (mw != -INFINITY) {
-          const float sc = fast_exp2(mw - M);
-          L += s_l[ww * 8 + gg] * sc;
-          O += s_o[(ww * 8 + gg) * kHD + d] * sc;
-        }
-      }
-      const size_t hq = (size_t)h * a.G + gg;
-      a.part_o[((size_t)c * a.Hq + hq) * kHD + d] = O;
-      if (d == 0) {
-        a.part_ml[((size_t)c * a.Hq + hq) * 2] = M;
-        a.part_ml[((size_t)c * a.Hq + hq) * 2 + 1] = L;
-      }
-    }
-    __syncthreads();  // scratch is reused by the next item's cp.async
-  }
-}
-
-// Merge the chunk partials of one (sequence, q head): grid (B, Hq), 128 threads.
-__global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeArgs a) {
-  const int b = blockIdx.x, hq = blockIdx.y, d = threadIdx.x;
-  const int c0 = a.chunk_start[b], c1 = a.chunk_start[b + 1];
-  if (c1 <= c0) return;  // padded row (q_len <= 0) or empty context
-  float M = -INFINITY;
-  for (int c = c0; c < c1; ++c) M = fmaxf(M, a.part_ml[((size_t)c * a.Hq + hq) * 2]);
-  float L = 0.f, O = 0.f;
-  for (int c = c0; c < c1; ++c) {
-    const float m = a.part_ml[((size_t)c * a.Hq + hq) * 2];
-    if (m == -INFINITY) continue;
-    const float sc = fast_exp2(m - M);
-    L += a.part_ml[((size_t)c * a.Hq + hq) * 2 + 1] * sc;
-    O += a.part_o[((size_t)c * a.Hq + hq) * kHD + d] * sc;
-  }
-  const float r = L > 0.f ? O / L : 0.f;
-  a.out[(size_t)a.cu_q[b] * a.out_stride + (size_t)hq * kHD + d] = __float2bfloat16_rn(r);
 }
 
 // ---------------------------------------------------------------------------

@@ -15,6 +15,7 @@
 #include <string>
 
 #include "attention.cuh"
+#include "decode_attention.cuh"
 #include "common.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
@@ -406,9 +407,8 @@ int b200_argmax(const void* logits, long long stride, int rows, int V, long long
 int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_t* bytes) {
   if (!bytes || max_seqs < 0 || max_seqlen_k < 0 || Hq <= 0)
     return fail(B200_ERR_INVALID, "bad arguments");
-  const size_t chunks = (size_t)max_seqs * ((max_seqlen_k + kDecChunk - 1) / kDecChunk);
-  const size_t head = ((size_t)(max_seqs + 1) * sizeof(int) + 255) / 256 * 256;
-  *bytes = head + chunks * Hq * (kHD + 2) * sizeof(float);
+  const size_t items = (size_t)max_seqs * ((max_seqlen_k + kDecItem - 1) / kDecItem);
+  *bytes = (size_t)kDecTicketBytes + items * Hq * (kDecHD + 2) * sizeof(float);
   return B200_OK;
 }
 
@@ -432,11 +432,11 @@ int b200_paged_attention(const void* q, long long q_stride, const void* k, long 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int G = Hq / Hkv;
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
-  if (max_seqlen_q == 1 && block_tables && G <= 8 && B <= kMaxPlanSeqs) {
-    const size_t head = ((size_t)(B + 1) * sizeof(int) + 255) / 256 * 256;
-    if (!workspace || ws_bytes <= head || !aligned16(workspace))
+  if (max_seqlen_q == 1 && block_tables && G <= 8 && B <= kDecMaxSeqs && Hkv <= kDecMaxKvHeads &&
+      page % kDecItem == 0) {
+    if (!workspace || ws_bytes <= (size_t)kDecTicketBytes || !aligned16(workspace))
       return fail(B200_ERR_WORKSPACE, "attention: decode workspace missing or too small");
-    const size_t per_chunk = (size_t)Hq * (kHD + 2) * sizeof(float);
+    const size_t per_item = (size_t)Hq * (kDecHD + 2) * sizeof(float);
     DecodeArgs a{};
     a.q = static_cast<const __nv_bfloat16*>(q); a.q_stride = q_stride;
     a.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
@@ -445,20 +445,16 @@ int b200_paged_attention(const void* q, long long q_stride, const void* k, long 
     a.cu_q = cu_seqlens_q; a.cu_k = cu_seqlens_k;
     a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = G; a.page = page; a.num_slots = num_slots;
     a.scale_log2 = scale_log2;
-    a.cap_chunks = (long long)((ws_bytes - head) / per_chunk);
-    a.chunk_start = static_cast<int*>(workspace);
-    a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + head);
-    a.part_o = a.part_ml + (size_t)a.cap_chunks * Hq * 2;
+    a.tickets = static_cast<int*>(workspace);
+    a.cap_items = (long long)((ws_bytes - kDecTicketBytes) / per_item);
+    a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + kDecTicketBytes);
+    a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
     a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
     a.err = ds->err;
-    const int smem = 65536 + ((B + 1) + 8) * (int)sizeof(int);
+    const int smem = dec_smem_bytes();
     if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
-    const long long bound = (long long)B * ((max_seqlen_k + kDecChunk - 1) / kDecChunk) * Hkv;
-    const int blocks = (int)std::max(1LL, std::min<long long>(bound, (long long)ds->num_sms * 3));
-    decode_attn_kernel<<<blocks, 128, smem, st>>>(a);
-    if (int r = check_launch("decode_attn_kernel")) return r;
-    decode_combine_kernel<<<dim3(B, Hq), 128, 0, st>>>(a);
-    return check_launch("decode_combine_kernel");
+    decode_attn_kernel<<<ds->num_sms, kDecWarps * 32, smem, st>>>(a);
+    return check_launch("decode_attn_kernel");
   }
   PrefillArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q); a.q_stride = q_stride;

@@ -125,13 +125,16 @@ _workspaces: dict[tuple[int, str], torch.Tensor] = {}
 
 
 def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
+    """Zero-filled on (re)allocation: the attention workspace starts with the
+    per-(sequence, kv head) tickets of the fused decode combine, which must be
+    zero before the first call (every call leaves them zero)."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError(f"workspace '{kind}' must be sized before CUDA-graph capture "
                                f"({nbytes} bytes requested)")
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _workspaces[key] = buf
     return buf
 

@@ -255,6 +255,23 @@ def test_decode_attention_paged(Hq, Hkv):
     assert L.rel_err(out.cpu(), ref) <= 2e-2
 
 
+def test_decode_attention_long_and_repeated():
+    """Sequences of > 32 items (the merge loops in rounds) and two calls in a
+    row (the per-sequence tickets of the fused merge must reset)."""
+    from src import b200
+    lens_k = [9000, 8193, 256, 511, 33]
+    q, kc, vc, bt, cu_q, cu_k = _paged_case([1] * 5, lens_k, 32, 8, seed=31)
+    scale = 128 ** -0.5
+    ref = L.varlen_attention(q, None, None, cu_q, cu_k, scale, kc, vc, bt)
+    args = (q.to(DEV), None, None, kc.to(DEV), vc.to(DEV), cu_q.to(DEV), cu_k.to(DEV), 1,
+            max(lens_k), scale, bt.to(DEV))
+    out1 = b200.paged_attention(*args)
+    out2 = b200.paged_attention(*args)
+    torch.cuda.synchronize()
+    assert L.rel_err(out1.cpu(), ref) <= 2e-2
+    assert torch.equal(out1, out2)
+
+
 def test_decode_attention_graph_padding():
     """CUDA-graph replay pads cu_seqlens with 0 and block tables with -1
     (src/engine/model_runner.py:248-257): padded rows must be skipped."""
