@@ -143,6 +143,7 @@ int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_
 /* Causal (bottom-right aligned) varlen GQA attention, head_dim 128.
  * Replaces src/layers/attention.py:93-104 (flash_attn_varlen_func with
  * cu_seqlens_q/k, max_seqlen_q/k, softmax_scale, causal=True, block_table).
+ *  - q: num_q_rows token rows of Hq x 128, q_stride elements apart.
  *  - block_tables != NULL: K/V from the paged cache [num_blocks, page, Hkv,
  *    128] (int32 block_tables: B rows of bt_width entries, bt_stride apart,
  *    -1 padded; a key past the row's width or in a -1 block is read as zero
@@ -156,7 +157,8 @@ int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_
  *    per-(sequence, kv head) tickets that must be zero before the first call
  *    and are zero again after every call; the rest is per-call scratch.
  *    Calls that share a workspace must not overlap on the GPU. */
-int b200_paged_attention(const void* q, long long q_stride, const void* k, long long k_stride,
+int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, const void* k,
+                         long long k_stride,
                          const void* v, long long v_stride, const void* k_cache,
                          const void* v_cache, long long num_slots, const int* block_tables,
                          int bt_stride, int bt_width, const int* cu_seqlens_q, const int* cu_seqlens_k, int B,

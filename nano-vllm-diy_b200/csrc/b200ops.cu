@@ -126,6 +126,24 @@ int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
   return B200_OK;
 }
 
+// 3-D bf16 tensor map: dims {d0 (contiguous), d1, d2} with byte strides
+// {s1, s2} for d1 / d2, box {b0, b1, b2}, 128-byte swizzle, zero fill outside.
+int make_tmap_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t s1_bytes, uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1_bytes, s2_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return B200_OK;
+}
+
 // ---------------------------------------------------------------------------
 // GEMM planning
 // ---------------------------------------------------------------------------
@@ -412,7 +430,8 @@ int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_
   return B200_OK;
 }
 
-int b200_paged_attention(const void* q, long long q_stride, const void* k, long long k_stride,
+int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, const void* k,
+                         long long k_stride,
                          const void* v, long long v_stride, const void* k_cache,
                          const void* v_cache, long long num_slots, const int* block_tables,
                          int bt_stride, int bt_width, const int* cu_seqlens_q, const int* cu_seqlens_k, int B,
@@ -436,14 +455,24 @@ int b200_paged_attention(const void* q, long long q_stride, const void* k, long 
       page % kDecItem == 0) {
     if (!workspace || ws_bytes <= (size_t)kDecTicketBytes || !aligned16(workspace))
       return fail(B200_ERR_WORKSPACE, "attention: decode workspace missing or too small");
+    if (num_q_rows <= 0) return fail(B200_ERR_INVALID, "attention: num_q_rows must be positive");
     const size_t per_item = (size_t)Hq * (kDecHD + 2) * sizeof(float);
+    CUtensorMap tmK, tmV, tmQ;
+    const int qbox = Hq < 8 ? Hq : 8;
+    if (int r = make_tmap_3d(&tmK, k_cache, kDecHD, Hkv, (uint64_t)num_slots, kDecHD * 2,
+                             (uint64_t)Hkv * kDecHD * 2, 64, 1, kDecTile))
+      return r;
+    if (int r = make_tmap_3d(&tmV, v_cache, kDecHD, Hkv, (uint64_t)num_slots, kDecHD * 2,
+                             (uint64_t)Hkv * kDecHD * 2, 64, 1, kDecTile))
+      return r;
+    if (int r = make_tmap_3d(&tmQ, q, kDecHD, Hq, (uint64_t)num_q_rows, kDecHD * 2,
+                             (uint64_t)q_stride * 2, 64, (uint32_t)qbox, 1))
+      return r;
     DecodeArgs a{};
-    a.q = static_cast<const __nv_bfloat16*>(q); a.q_stride = q_stride;
-    a.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
-    a.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
     a.block_tables = block_tables; a.bt_stride = bt_stride; a.bt_width = bt_width;
     a.cu_q = cu_seqlens_q; a.cu_k = cu_seqlens_k;
-    a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = G; a.page = page; a.num_slots = num_slots;
+    a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = G; a.page = page; a.q_box_rows = qbox;
+    a.num_slots = num_slots;
     a.scale_log2 = scale_log2;
     a.tickets = static_cast<int*>(workspace);
     a.cap_items = (long long)((ws_bytes - kDecTicketBytes) / per_item);
@@ -453,7 +482,7 @@ int b200_paged_attention(const void* q, long long q_stride, const void* k, long 
     a.err = ds->err;
     const int smem = dec_smem_bytes();
     if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
-    decode_attn_kernel<<<ds->num_sms, kDecWarps * 32, smem, st>>>(a);
+    decode_attn_kernel<<<ds->num_sms, kDecWarps * 32, smem, st>>>(tmK, tmV, tmQ, a);
     return check_launch("decode_attn_kernel");
   }
   PrefillArgs a{};

@@ -10,20 +10,21 @@
 //           reference's block size (runner_config.py:39), so an item lies in
 //           one physical block.  The G = Hq / Hkv query heads that share the
 //           kv head are the rows of one m16n8k16 MMA.
-//   warp  = owns whole items; a persistent grid (one 4-warp CTA per SM)
-//           hands items to warps round-robin.  Each warp runs its own
-//           3-stage cp.async ring of 32-token K/V tiles (+ the item's Q rows
-//           with its first tile) that keeps streaming across item
-//           boundaries, so loads stay in flight while the warp computes and
-//           no CTA-wide barrier is ever taken.
-//   combine = a sequence spanning several items writes per-item partials
+//   warp  = owns whole items, taken from a global atomic counter (dynamic
+//           scheduling: no tail from uneven sequence lengths).  Each warp
+//           runs its own 3-stage ring of 32-token K/V tiles (+ the item's Q
+//           rows with its first tile) loaded by TMA (cp.async.bulk.tensor,
+//           128-byte swizzle, one mbarrier per stage, issued by lane 0), so
+//           the ring keeps streaming across item boundaries and no CTA-wide
+//           barrier is taken after the start.
+//   merge = a sequence spanning several items writes per-item partials
 //           (m, l, o); the warp that finishes the last item of (sequence,
 //           kv head) -- found with an atomic ticket -- merges them and writes
-//           the output, then resets the ticket for the next call.  A
-//           single-item sequence writes its output directly.
-// The launch shape depends only on B and the SM count, never on the context
-// lengths, which are read from cu_seqlens_k on the device (CUDA-graph safe;
-// rows with q length <= 0 are graph padding and are skipped).
+//           the output, then resets the ticket.  A single-item sequence
+//           writes its output directly.
+// The launch shape depends only on the SM count; context lengths are read
+// from cu_seqlens_k on the device (CUDA-graph safe; rows with q length <= 0
+// are graph padding and are skipped).
 #pragma once
 #include "common.cuh"
 
@@ -36,26 +37,24 @@ constexpr int kDecStages = 3;
 constexpr int kDecWarps = 4;
 constexpr int kDecMaxSeqs = 1024;       // plan / ticket capacity
 constexpr int kDecMaxKvHeads = 64;
-constexpr int kDecStageBytes = 2 * kDecTile * 256 + 8 * 256;   // K + V + Q rows
+// stage: K [2 halves][32 rows][128 B] | V same | Q [2 halves][8 rows][128 B]
+constexpr int kDecStK = 0, kDecStV = 8192, kDecStQ = 16384;
+constexpr int kDecStageBytes = 18432;
 constexpr int kDecWarpBytes = kDecStages * kDecStageBytes;
-constexpr int kDecTicketBytes = kDecMaxSeqs * kDecMaxKvHeads * 4;  // workspace head
-
-struct DecTile;
-__host__ __device__ constexpr int dec_smem_bytes();
+// workspace head: tickets [kDecMaxSeqs * kDecMaxKvHeads] ints, then the
+// scheduler words {next item, warps done}; all zero between calls
+constexpr int kDecSchedOffset = kDecMaxSeqs * kDecMaxKvHeads * 4;
+constexpr int kDecTicketBytes = kDecSchedOffset + 256;
 
 struct DecodeArgs {
-  const __nv_bfloat16* q;
-  long long q_stride;
-  const __nv_bfloat16* k_cache;
-  const __nv_bfloat16* v_cache;
   const int* block_tables;
   int bt_stride, bt_width;
   const int* cu_q;
   const int* cu_k;
-  int B, Hq, Hkv, G, page;
+  int B, Hq, Hkv, G, page, q_box_rows;
   long long num_slots;
   float scale_log2;      // softmax_scale * log2(e)
-  int* tickets;          // [kDecMaxSeqs * kDecMaxKvHeads], zero between calls
+  int* tickets;          // workspace head (see kDecTicketBytes)
   float* part_ml;        // [cap_items][Hq][2]
   float* part_o;         // [cap_items][Hq][128]
   long long cap_items;
@@ -66,29 +65,47 @@ struct DecodeArgs {
 
 struct DecTile {
   int b, h, c, npages, qrow;
-  int tok0;     // first token of the tile inside the sequence
   int ntok;     // valid tokens in the tile
   int first, last;
-  long long row0;  // cache row (slot) of token tok0, -1 if the block is invalid
+  long long row;  // cache row (slot) of the tile's first token
 };
 
 __host__ __device__ constexpr int dec_smem_bytes() {
-  return kDecWarps * kDecWarpBytes + kDecWarps * kDecStages * (int)sizeof(DecTile) +
-         (8 + kDecMaxSeqs + 1) * (int)sizeof(int);
+  return 1024 + kDecWarps * kDecWarpBytes + kDecWarps * kDecStages * 8 +
+         kDecWarps * kDecStages * (int)sizeof(DecTile) + (8 + kDecMaxSeqs + 1) * (int)sizeof(int);
 }
 
-__device__ __forceinline__ uint32_t dswz(int r, int ch) {
-  return (uint32_t)(r * 256 + ((ch ^ (r & 7)) << 4));
+// byte offset of 16-byte chunk `ch` (0..15 over 128 dims) of row `r` in a
+// [2 halves][rows][128 B] TMA tile with the 128-byte swizzle
+__device__ __forceinline__ uint32_t tswz(int half_bytes, int r, int ch) {
+  return (uint32_t)((ch >> 3) * half_bytes + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(128, 1)
+    decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const __grid_constant__ CUtensorMap tmQ, const DecodeArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // layout: [warp rings][tile descriptors][scan scratch][plan]
-  DecTile* s_desc = reinterpret_cast<DecTile*>(smem + kDecWarps * kDecWarpBytes) + warp * kDecStages;
-  int* s_scan = reinterpret_cast<int*>(smem + kDecWarps * kDecWarpBytes +
+  // layout: [warp rings][mbarriers][tile descriptors][scan scratch][plan]
+  uint64_t* s_bar = reinterpret_cast<uint64_t*>(smem + kDecWarps * kDecWarpBytes) + warp * kDecStages;
+  DecTile* s_desc = reinterpret_cast<DecTile*>(smem + kDecWarps * kDecWarpBytes + kDecWarps * kDecStages * 8) +
+                    warp * kDecStages;
+  int* s_scan = reinterpret_cast<int*>(smem + kDecWarps * kDecWarpBytes + kDecWarps * kDecStages * 8 +
                                        kDecWarps * kDecStages * sizeof(DecTile));
   int* s_start = s_scan + 8;
+  int* sched = a.tickets + kDecSchedOffset / 4;   // {next item, warps done}
+
+  if (lane == 0) {
+    for (int i = 0; i < kDecStages; ++i) mbar_init(&s_bar[i], 1);
+    fence_mbar_init();
+  }
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmQ);
+  }
 
   // ---- plan: exclusive prefix sum of items per sequence (identical in every CTA)
   {
@@ -127,18 +144,26 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
     return;
   }
   const int items = total_chunks * a.Hkv;
-  const int gwarp = blockIdx.x * kDecWarps + warp;
   const int nwarps = gridDim.x * kDecWarps;
-
-  uint8_t* wbase = smem + warp * kDecWarpBytes;
-  const uint32_t wsmem = smem_u32(wbase);
+  const uint32_t wsmem = smem_u32(smem + warp * kDecWarpBytes);
 
   // ---- tile iterator (uniform across the warp)
-  int it_w = gwarp;       // current item
-  int it_k = 0;           // next tile inside it
-  int it_tiles = 0;
+  bool more = true;       // the warp may still take items
+  int it_k = 0, it_tiles = 0;
   DecTile cur{};
-  auto decode_item = [&](int w) {
+  auto grab_item = [&]() {
+    int w = 0;
+    if (lane == 0) w = atomicAdd(&sched[0], 1);
+    w = __shfl_sync(0xffffffffu, w, 0);
+    if (w >= items) {
+      more = false;
+      if (lane == 0 && atomicAdd(&sched[1], 1) == nwarps - 1) {
+        // every warp has left the queue: reset it for the next call
+        atomicExch(&sched[0], 0);
+        atomicExch(&sched[1], 0);
+      }
+      return;
+    }
     const int c = w / a.Hkv;
     const int h = w - c * a.Hkv;
     int lo = 0, hi = a.B - 1;
@@ -147,62 +172,52 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
       if (s_start[mid] <= c) lo = mid; else hi = mid - 1;
     }
     const int b = lo;
-    const int p = c - s_start[b];
+    const int j0 = (c - s_start[b]) * kDecItem;
     const int nk = a.cu_k[b + 1] - a.cu_k[b];
-    cur.b = b; cur.h = h; cur.c = c;
-    cur.npages = s_start[b + 1] - s_start[b];
-    cur.qrow = a.cu_q[b];
-    const int j0 = p * kDecItem;
     const int ntok_item = min(kDecItem, nk - j0);
     const int col = j0 / a.page;
     const long long blk = col < a.bt_width ? a.block_tables[(size_t)b * a.bt_stride + col] : -1;
     const long long row = blk * a.page + (j0 % a.page);
-    cur.row0 = (blk < 0 || row + ntok_item > a.num_slots) ? -1 : row;
-    if (cur.row0 < 0 && lane == 0) raise_error(a.err, ERR_BAD_INDEX);
-    cur.tok0 = j0;
-    cur.ntok = ntok_item;  // item-level for now
+    cur.b = b; cur.h = h; cur.c = c;
+    cur.npages = s_start[b + 1] - s_start[b];
+    cur.qrow = a.cu_q[b];
+    cur.ntok = ntok_item;
+    cur.row = (blk < 0 || row + ntok_item > a.num_slots) ? -1 : row;
+    if (cur.row < 0 && lane == 0) raise_error(a.err, ERR_BAD_INDEX);
     it_tiles = (ntok_item + kDecTile - 1) / kDecTile;
     it_k = 0;
   };
-  if (it_w < items) decode_item(it_w);
+  grab_item();
 
   int issued = 0, valid_issued = 0;
   auto issue_next = [&]() {
-    if (it_w < items) {
+    if (more) {
       const int s = issued % kDecStages;
       DecTile d = cur;
-      d.tok0 = cur.tok0 + it_k * kDecTile;
-      d.ntok = min(kDecTile, cur.ntok - it_k * kDecTile);
+      // an invalid block loads rows 0.. of the cache and masks every token
+      d.ntok = cur.row < 0 ? 0 : min(kDecTile, cur.ntok - it_k * kDecTile);
       d.first = it_k == 0;
       d.last = it_k == it_tiles - 1;
-      if (lane == 0) s_desc[s] = d;
-      const uint32_t sK = wsmem + s * kDecStageBytes;
-      const uint32_t sV = sK + kDecTile * 256;
-      const uint32_t sQ = sV + kDecTile * 256;
-      const long long row_tile = d.row0 < 0 ? -1 : d.row0 + (long long)it_k * kDecTile;
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const int idx = lane + 32 * i;
-        const int r = idx >> 4, ch = idx & 15;
-        const bool valid = r < d.ntok && row_tile >= 0;
-        const size_t off = valid ? ((size_t)(row_tile + r) * a.Hkv + d.h) * kDecHD + ch * 8 : 0;
-        cp_async_16_zfill(sK + dswz(r, ch), a.k_cache + off, valid);
-        cp_async_16_zfill(sV + dswz(r, ch), a.v_cache + off, valid);
-      }
-      if (d.first) {
-        for (int idx = lane; idx < a.G * 16; idx += 32) {
-          const int g = idx >> 4, ch = idx & 15;
-          cp_async_16(sQ + g * 256 + ch * 16,
-                      a.q + (size_t)d.qrow * a.q_stride + (size_t)(d.h * a.G + g) * kDecHD + ch * 8);
+      d.row = cur.row < 0 ? 0 : cur.row + (long long)it_k * kDecTile;
+      if (lane == 0) {
+        s_desc[s] = d;
+        const uint32_t st = wsmem + s * kDecStageBytes;
+        const uint32_t bar = smem_u32(&s_bar[s]);
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&s_bar[s], 4 * 4096 + (d.first ? 2 * 128 * a.q_box_rows : 0));
+        const int r = (int)d.row;
+        tma_load_3d(st + kDecStK, &tmK, bar, 0, d.h, r);
+        tma_load_3d(st + kDecStK + 4096, &tmK, bar, 64, d.h, r);
+        tma_load_3d(st + kDecStV, &tmV, bar, 0, d.h, r);
+        tma_load_3d(st + kDecStV + 4096, &tmV, bar, 64, d.h, r);
+        if (d.first) {
+          tma_load_3d(st + kDecStQ, &tmQ, bar, 0, d.h * a.G, d.qrow);
+          tma_load_3d(st + kDecStQ + 1024, &tmQ, bar, 64, d.h * a.G, d.qrow);
         }
       }
       ++valid_issued;
-      if (++it_k == it_tiles) {
-        it_w += nwarps;
-        if (it_w < items) decode_item(it_w);
-      }
+      if (++it_k == it_tiles) grab_item();
     }
-    cp_async_commit();
     ++issued;
   };
 
@@ -215,25 +230,41 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
   uint32_t qa[8][4];
   float o[16][4];
   float m_run = -INFINITY, l_run = 0.f;
+  int consumed = 0;
 
   for (int t = 0; t < valid_issued; ++t) {
-    cp_async_wait<1>();
     __syncwarp();
-    issue_next();
+    issue_next();  // refills the stage of tile t - 1
     const int s = t % kDecStages;
+    const uint32_t ph = (uint32_t)(t / kDecStages) & 1u;
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(&s_bar[s], ph, a.err) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) break;
+    consumed = t + 1;
+    mbar_wait(&s_bar[s], ph, a.err);  // every lane observes the completed phase
     const DecTile d = s_desc[s];
-    const uint32_t sK = wsmem + s * kDecStageBytes;
-    const uint32_t sV = sK + kDecTile * 256;
-    const uint8_t* sQp = wbase + s * kDecStageBytes + 2 * kDecTile * 256;
+    const uint32_t sK = wsmem + s * kDecStageBytes + kDecStK;
+    const uint32_t sV = wsmem + s * kDecStageBytes + kDecStV;
+    const uint32_t sQ = wsmem + s * kDecStageBytes + kDecStQ;
+    if (d.ntok < kDecTile) {
+      // rows past the sequence hold other data of the block (possibly never
+      // written): zero V there so that P = 0 cannot meet a NaN
+      uint8_t* vrow = smem + warp * kDecWarpBytes + s * kDecStageBytes + kDecStV;
+      for (int idx = lane; idx < (kDecTile - d.ntok) * 16; idx += 32) {
+        const int r = d.ntok + (idx >> 4), ch = idx & 15;
+        *reinterpret_cast<uint4*>(vrow + tswz(4096, r, ch)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
 
     if (d.first) {
+      // A fragments of Q: rows 0-7 = heads (rows >= G unused), rows 8-15 zero
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int dd = ks * 16 + 2 * (lane & 3);
-        qa[ks][0] = live_row ? *reinterpret_cast<const uint32_t*>(sQp + g * 256 + dd * 2) : 0u;
-        qa[ks][1] = 0u;
-        qa[ks][2] = live_row ? *reinterpret_cast<const uint32_t*>(sQp + g * 256 + (dd + 8) * 2) : 0u;
-        qa[ks][3] = 0u;
+      for (int kp = 0; kp < 4; ++kp) {
+        ldmatrix_x4(sQ + tswz(1024, rin, 4 * kp + mi), qa[2 * kp][0], qa[2 * kp][2],
+                    qa[2 * kp + 1][0], qa[2 * kp + 1][2]);
+        qa[2 * kp][1] = qa[2 * kp][3] = qa[2 * kp + 1][1] = qa[2 * kp + 1][3] = 0u;
       }
 #pragma unroll
       for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
@@ -250,7 +281,7 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
         uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(sK + dswz(nt * 8 + rin, 4 * kp + mi), b0, b1, b2, b3);
+        ldmatrix_x4(sK + tswz(4096, nt * 8 + rin, 4 * kp + mi), b0, b1, b2, b3);
         mma_bf16_16816(sc[nt], qa[2 * kp], b0, b1);
         mma_bf16_16816(sc[nt], qa[2 * kp + 1], b2, b3);
       }
@@ -274,17 +305,17 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
     float ls = 0.f;
     // P enters the PV MMA as bf16 hi + lo parts (hi = bf16(p), lo = bf16(p - hi)):
     // ~16 significant bits of p instead of 8.
-    uint32_t ph[2][4], pl[2][4];
+    uint32_t ph2[2][4], pl[2][4];
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
-      const float p0 = fast_exp2(sc[nt][0] - m_new);
-      const float p1 = fast_exp2(sc[nt][1] - m_new);
+      const float p0 = m_new == -INFINITY ? 0.f : fast_exp2(sc[nt][0] - m_new);
+      const float p1 = m_new == -INFINITY ? 0.f : fast_exp2(sc[nt][1] - m_new);
       ls += p0 + p1;
       const uint32_t hk = pack_bf16x2(p0, p1);
       const float2 hf = unpack_bf16x2(hk);
       const uint32_t lk = pack_bf16x2(p0 - hf.x, p1 - hf.y);
       const int kp = nt >> 1, hiw = (nt & 1) * 2;
-      ph[kp][hiw] = hk; ph[kp][hiw + 1] = 0u;
+      ph2[kp][hiw] = hk; ph2[kp][hiw + 1] = 0u;
       pl[kp][hiw] = lk; pl[kp][hiw + 1] = 0u;
     }
     ls += __shfl_xor_sync(0xffffffffu, ls, 1);
@@ -301,9 +332,9 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
 #pragma unroll
       for (int dp = 0; dp < 8; ++dp) {
         uint32_t v0, v1, v2, v3;
-        ldmatrix_x4_trans(sV + dswz(kp * 16 + 8 * (mi & 1) + rin, 2 * dp + (mi >> 1)), v0, v1, v2, v3);
-        mma_bf16_16816(o[2 * dp], ph[kp], v0, v1);
-        mma_bf16_16816(o[2 * dp + 1], ph[kp], v2, v3);
+        ldmatrix_x4_trans(sV + tswz(4096, kp * 16 + 8 * (mi & 1) + rin, 2 * dp + (mi >> 1)), v0, v1, v2, v3);
+        mma_bf16_16816(o[2 * dp], ph2[kp], v0, v1);
+        mma_bf16_16816(o[2 * dp + 1], ph2[kp], v2, v3);
         mma_bf16_16816(o[2 * dp], pl[kp], v0, v1);
         mma_bf16_16816(o[2 * dp + 1], pl[kp], v2, v3);
       }
@@ -338,28 +369,48 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
     ticket = __shfl_sync(0xffffffffu, ticket, 0);
     if (ticket != d.npages - 1) continue;
     __threadfence();
-    // this warp merges the npages partials of (b, h)
+    // this warp merges the npages partials of (b, h): every lane loads the
+    // (m, l) of one item at a time and the partial rows are read 8 items per
+    // batch, so the merge is not a chain of dependent L2 round trips
     const int c0 = s_start[d.b];
+    const int np = d.npages;
     for (int gg = 0; gg < a.G; ++gg) {
       const size_t hqq = (size_t)d.h * a.G + gg;
       float M = -INFINITY;
-      for (int p = lane; p < d.npages; p += 32)
-        M = fmaxf(M, __ldcg(a.part_ml + ((size_t)(c0 + p) * a.Hq + hqq) * 2));
+      for (int p0 = 0; p0 < np; p0 += 32) {
+        if (p0 + lane < np) M = fmaxf(M, __ldcg(a.part_ml + ((size_t)(c0 + p0 + lane) * a.Hq + hqq) * 2));
+      }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
       float L = 0.f;
-      for (int p = lane; p < d.npages; p += 32) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + ((size_t)(c0 + p) * a.Hq + hqq) * 2));
-        L += fast_exp2(ml.x - M) * ml.y;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p0 = 0; p0 < np; p0 += 32) {
+        float w = 0.f;
+        if (p0 + lane < np) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + ((size_t)(c0 + p0 + lane) * a.Hq + hqq) * 2));
+          w = fast_exp2(ml.x - M);
+          L += w * ml.y;
+        }
+        const int cnt = min(32, np - p0);
+        for (int j = 0; j < cnt; j += 8) {
+          float4 ov[8];
+          float wj[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            wj[u] = __shfl_sync(0xffffffffu, w, j + u);
+            ov[u] = j + u < cnt
+                        ? __ldcg(reinterpret_cast<const float4*>(a.part_o + ((size_t)(c0 + p0 + j + u) * a.Hq + hqq) * kDecHD) + lane)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            acc.x += wj[u] * ov[u].x; acc.y += wj[u] * ov[u].y;
+            acc.z += wj[u] * ov[u].z; acc.w += wj[u] * ov[u].w;
+          }
+        }
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = 0; p < d.npages; ++p) {
-        const float w = fast_exp2(__ldcg(a.part_ml + ((size_t)(c0 + p) * a.Hq + hqq) * 2) - M);
-        const float4 ov = __ldcg(reinterpret_cast<const float4*>(a.part_o + ((size_t)(c0 + p) * a.Hq + hqq) * kDecHD) + lane);
-        acc.x += w * ov.x; acc.y += w * ov.y; acc.z += w * ov.z; acc.w += w * ov.w;
-      }
       const float inv = L > 0.f ? 1.f / L : 0.f;
       uint2 packed;
       packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
@@ -368,7 +419,12 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeArgs a)
     }
     if (lane == 0) atomicExch(a.tickets + (size_t)d.b * a.Hkv + d.h, 0);
   }
-  cp_async_wait<0>();
+  // drain: every issued tile has landed before the CTA's shared memory is released
+  if (lane == 0) {
+    for (int t = consumed; t < valid_issued; ++t)
+      mbar_wait(&s_bar[t % kDecStages], (uint32_t)(t / kDecStages) & 1u, a.err);
+  }
+  __syncwarp();
 }
 
 }  // namespace b200

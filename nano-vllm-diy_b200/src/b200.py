@@ -50,7 +50,7 @@ _SIGNATURES = {
     "b200_embedding": ([_c_void_p, _c_void_p, _c_void_p, _i, _i, _ll, _ll, _c_void_p], _i),
     "b200_argmax": ([_c_void_p, _ll, _i, _i, _c_void_p, _c_void_p], _i),
     "b200_attention_workspace_bytes": ([_i, _i, _i, ctypes.POINTER(_sz)], _i),
-    "b200_paged_attention": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _ll, _c_void_p,
+    "b200_paged_attention": ([_c_void_p, _ll, _i, _c_void_p, _ll, _c_void_p, _ll, _c_void_p,
                               _c_void_p, _ll, _c_void_p, _i, _i, _c_void_p, _c_void_p, _i, _i, _i,
                               _i, _i, _i, _f, _c_void_p, _ll, _c_void_p, _sz, _c_void_p], _i),
 }
@@ -367,7 +367,7 @@ def paged_attention(q: torch.Tensor, k: torch.Tensor | None, v: torch.Tensor | N
         ws = workspace("attn", nbytes, q.device)
         nbytes = ws.numel()
     _check(lib.b200_paged_attention(
-        _p(q), q.stride(0), _p(k_arg), ks, _p(v_arg), vs,
+        _p(q), q.stride(0), T, _p(k_arg), ks, _p(v_arg), vs,
         _p(k_cache) if block_table is not None else None,
         _p(v_cache) if block_table is not None else None, num_slots, _p(block_table), bt_stride, bt_width,
         _p(cu_seqlens_q), _p(cu_seqlens_k), B, int(max_seqlen_q), int(max_seqlen_k), Hq, Hkv, page,
