@@ -57,9 +57,9 @@ int b200_device_error(unsigned* out, int clear);
  * Linear layers
  * ------------------------------------------------------------------------ */
 
-/* Bytes of fp32 split-K workspace b200_linear would use for this shape
- * (0 when it does not split K).  A smaller workspace is allowed: the kernel
- * then splits less. */
+/* Workspace bytes b200_linear needs for this shape: always 0 (split-K
+ * partials are summed on chip through cluster shared memory); kept so that
+ * callers can size buffers without knowing the kernel's tiling. */
 int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes);
 
 /* y[T, N] = x[T, K] * w[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate,
@@ -67,7 +67,8 @@ int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes);
  *   src/layers/linear.py:74-75   ColumnParallelLinear.forward
  *   src/layers/linear.py:169-170 RowParallelLinear.forward (per-rank part)
  *   src/layers/llm_head.py:64    ParallelLMHead.forward
- * K, ldx and ldw must be multiples of 8; x and w 16-byte aligned. */
+ * K, ldx and ldw must be multiples of 8; x and w 16-byte aligned.
+ * `workspace` / `ws_bytes` are accepted and unused (may be NULL / 0). */
 int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
                 void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
                 b200_stream_t stream);
@@ -77,7 +78,8 @@ int b200_linear(const void* x, long long ldx, const void* w, long long ldw, cons
  *   src/models/qwen3.py:119-121 (gate_up_proj -> act_fn) =
  *   src/layers/linear.py:74-75 + src/layers/activation.py:6-10.
  * w is [2I, K] with rows [gate ; up] exactly as MergedColumnParallelLinear
- * stores them (src/layers/linear.py:89-102). */
+ * stores them (src/layers/linear.py:89-102).  I must be a multiple of 64
+ * (B200_ERR_UNSUPPORTED otherwise); workspace is unused. */
 int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long long ldw, void* y,
                              long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
                              b200_stream_t stream);

@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -153,90 +154,106 @@ struct GemmPlan {
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
-GemmPlan plan_gemm(int T, int N, int K, bool silu_tiles, int num_sms, size_t ws_bytes,
-                   int ws_cols) {
+// Two CTAs per SM: each CTA's ring stays under ~110 KB, so the epilogue of
+// one CTA overlaps the main loop of the other.
+constexpr int kGemmSmemBudget = 110 * 1024;
+
+bool gemm_debug() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("B200_GEMM_DEBUG");
+    v = (e && *e && *e != '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// Optional override "BN,S,budget_kb" from B200_GEMM_CONFIG (tuning sweeps).
+bool gemm_forced(int* bn, int* s, int* budget) {
+  const char* e = getenv("B200_GEMM_CONFIG");
+  if (!e || !*e) return false;
+  return sscanf(e, "%d,%d,%d", bn, s, budget) == 3;
+}
+
+GemmPlan plan_gemm(DeviceState* ds, int T, int N, int K, bool silu_tiles) {
   GemmPlan p{};
-  p.BN = T <= 256 ? max(32, round_up(T, 32)) : 256;
+  int f_bn = 0, f_s = 0, f_budget = 0;
+  const bool forced = gemm_forced(&f_bn, &f_s, &f_budget);
+  p.BN = std::min(128, std::max(32, round_up(T, 32)));
+  if (forced) p.BN = std::min(256, std::max(32, std::min(f_bn, round_up(T, 32))));
   p.token_tiles = (T + p.BN - 1) / p.BN;
   p.n_tiles = silu_tiles ? (N / 2 + 63) / 64 : (N + kGemmBM - 1) / kGemmBM;
   p.num_kb = (K + kGemmBK - 1) / kGemmBK;
-  const int tiles = p.n_tiles * p.token_tiles;
-  int splits = 1;
-  if (tiles < num_sms) {
-    splits = min(p.num_kb, (2 * num_sms + tiles - 1) / tiles);
-    // every split must own at least 4 K blocks
-    splits = max(1, min(splits, p.num_kb / 4));
-    // and the fp32 partials must fit the caller's workspace
-    while (splits > 1 && (size_t)splits * T * ws_cols * sizeof(float) > ws_bytes) --splits;
-  }
-  p.kb_per_split = (p.num_kb + splits - 1) / splits;
-  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
   const int stage = kGemmBM * kGemmBK * 2 + p.BN * kGemmBK * 2;
-  p.stages = max(2, min(kGemmMaxStages, (100 * 1024) / stage));
-  p.smem = p.stages * stage + 1024 + 256;
+  const int budget = forced ? f_budget * 1024 : kGemmSmemBudget;
+  p.stages = std::max(2, std::min(kGemmMaxStages, (budget - 2048) / stage));
+  while (p.stages * stage < p.BN * kGemmBM * 4) ++p.stages;  // ring holds the fp32 tile
+  p.smem = 1024 + p.stages * stage + 256;
   p.tmem_cols = 32;
   while (p.tmem_cols < p.BN) p.tmem_cols <<= 1;
+  // split K over a cluster when the tiles leave SMs idle: measured on the
+  // Qwen3-8B decode shapes (T = 256), 2-way splits win for K <= 8192 and
+  // 4-way for longer K; every rank keeps >= 8 K blocks
+  const int tiles = p.n_tiles * p.token_tiles;
+  int best_s = 1;
+  if (tiles < ds->num_sms) best_s = p.num_kb >= 128 ? 4 : 2;
+  while (best_s > 1 && p.num_kb / best_s < 8) --best_s;
+  if (gemm_debug())
+    fprintf(stderr, "[b200 gemm] T=%d N=%d K=%d BN=%d tiles=%d S=%d\n", T, N, K, p.BN, tiles, best_s);
+  if (forced) best_s = std::max(1, std::min(8, std::min(f_s, p.num_kb)));
+  p.kb_per_split = (p.num_kb + best_s - 1) / best_s;
+  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  if (gemm_debug())
+    fprintf(stderr, "[b200 gemm] -> T=%d N=%d K=%d BN=%d tiles=%d splits=%d stages=%d smem=%d\n", T, N,
+            K, p.BN, tiles, p.splits, p.stages, p.smem);
   return p;
 }
 
 int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const void* bias, void* y,
-             long long ldy, int T, int N, int K, bool silu, void* ws, size_t ws_bytes,
-             cudaStream_t st) {
+             long long ldy, int T, int N, int K, bool silu, cudaStream_t st) {
   if (T <= 0) return B200_OK;
   if (N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "linear: bad shape N=%d K=%d", N, K);
   if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K)
     return fail(B200_ERR_INVALID, "linear: K (%d) and row strides (%lld, %lld) must be multiples of 8", K, ldx, ldw);
   if (!aligned16(x) || !aligned16(w)) return fail(B200_ERR_INVALID, "linear: x and w must be 16-byte aligned");
-  if (silu && (N % 2 || ldy < N / 2)) return fail(B200_ERR_INVALID, "linear_silu: bad N=%d / ldy", N);
+  if (silu && (N % 2 || (N / 2) % 64 || ldy < N / 2))
+    return fail(B200_ERR_UNSUPPORTED, "linear_silu: I = %d must be a multiple of 64", N / 2);
   if (!silu && ldy < N) return fail(B200_ERR_INVALID, "linear: ldy < N");
   DeviceState* ds;
   if (int r = device_state(&ds)) return r;
-  GemmPlan p = plan_gemm(T, N, K, silu && (N / 2) % 64 == 0, ds->num_sms, ws ? ws_bytes : 0, N);
-  const bool fused_silu = silu && p.splits == 1 && (N / 2) % 64 == 0;
-  if (silu && !fused_silu) {
-    // silu via fp32 partials + reduce: plan over all N rows of W
-    p = plan_gemm(T, N, K, false, ds->num_sms, ws ? ws_bytes : 0, N);
-    if ((size_t)p.splits * T * N * sizeof(float) > ws_bytes || ws == nullptr) {
-      // force a single split through the reduce path
-      p.kb_per_split = p.num_kb;
-      p.splits = 1;
-      if ((size_t)T * N * sizeof(float) > ws_bytes || ws == nullptr)
-        return fail(B200_ERR_WORKSPACE, "linear_silu: workspace of %zu bytes too small (need %zu)",
-                    ws_bytes, (size_t)T * N * sizeof(float));
-    }
-  }
-  if (ws != nullptr && !aligned16(ws)) return fail(B200_ERR_INVALID, "linear: workspace must be 16-byte aligned");
+  const GemmPlan p = plan_gemm(ds, T, N, K, silu);
   CUtensorMap tmW, tmX;
   if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK,
-                        fused_silu ? 64u : (uint32_t)kGemmBM))
+                        silu ? 64u : (uint32_t)kGemmBM))
     return r;
   if (int r = make_tmap(&tmX, x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx, kGemmBK, (uint32_t)p.BN))
     return r;
   if (int r = ensure_smem(ds, 1u, gemm_tn_tcgen05_kernel, p.smem)) return r;
   GemmArgs a{};
   a.T = T; a.N = N; a.K = K; a.BN = p.BN; a.stages = p.stages; a.num_kb = p.num_kb;
-  a.kb_per_split = p.kb_per_split; a.tmem_cols = p.tmem_cols;
+  a.kb_per_split = p.kb_per_split; a.splits = p.splits; a.tmem_cols = p.tmem_cols;
+  a.epi = silu ? EPI_SILU : EPI_BF16;
+  a.vec_ok = aligned16(y) && (ldy % 8 == 0);
   a.y = static_cast<__nv_bfloat16*>(y); a.ldy = ldy;
-  a.ws = static_cast<float*>(ws);
   a.bias = static_cast<const __nv_bfloat16*>(bias);
   a.silu_inter = N / 2;
   a.err = ds->err;
-  const bool reduce = p.splits > 1 || (silu && !fused_silu);
-  a.epi = fused_silu ? EPI_SILU : (reduce ? EPI_F32 : EPI_BF16);
-  dim3 grid(p.n_tiles, p.token_tiles, p.splits);
-  gemm_tn_tcgen05_kernel<<<grid, kGemmThreads, p.smem, st>>>(tmW, tmX, a);
-  if (int r = check_launch("gemm_tn_tcgen05_kernel")) return r;
-  if (reduce) {
-    const int outN = silu ? N / 2 : N;
-    const long long vecs = (long long)T * (outN / 4);
-    const int blocks = (int)std::min<long long>((vecs + 255) / 256, (long long)ds->num_sms * 8);
-    splitk_reduce_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(ws), p.splits, T, N,
-                                                 static_cast<__nv_bfloat16*>(y), ldy,
-                                                 static_cast<const __nv_bfloat16*>(bias),
-                                                 silu ? EPI_SILU : EPI_BF16);
-    if (int r = check_launch("splitk_reduce_kernel")) return r;
-  }
-  return B200_OK;
+  cudaLaunchConfig_t cfg = {};
+  // token tiles fastest: the CTAs that share a W slab run side by side and the
+  // second read of each W block hits L2
+  cfg.gridDim = dim3(p.token_tiles, p.n_tiles, p.splits);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = p.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.splits > 1 ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tn_tcgen05_kernel, tmW, tmX, a);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
+  return check_launch("gemm_tn_tcgen05_kernel");
 }
 
 }  // namespace
@@ -271,23 +288,23 @@ int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes) {
   if (!bytes || T < 0 || N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "bad arguments");
   DeviceState* ds;
   if (int r = device_state(&ds)) return r;
-  const GemmPlan p = plan_gemm(T, N, K, false, ds->num_sms, (size_t)-1 / 2, N);
-  *bytes = p.splits > 1 ? (size_t)p.splits * T * N * sizeof(float) : 0;
+  (void)ds;
+  *bytes = 0;  // split-K partials are reduced on chip (cluster shared memory)
   return B200_OK;
 }
 
 int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
                 void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
                 b200_stream_t stream) {
-  return run_gemm(x, ldx, w, ldw, bias, y, ldy, T, N, K, false, workspace, ws_bytes,
-                  reinterpret_cast<cudaStream_t>(stream));
+  (void)workspace; (void)ws_bytes;
+  return run_gemm(x, ldx, w, ldw, bias, y, ldy, T, N, K, false, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long long ldw, void* y,
                              long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
                              b200_stream_t stream) {
-  return run_gemm(x, ldx, w, ldw, nullptr, y, ldy, T, 2 * I, K, true, workspace, ws_bytes,
-                  reinterpret_cast<cudaStream_t>(stream));
+  (void)workspace; (void)ws_bytes;
+  return run_gemm(x, ldx, w, ldw, nullptr, y, ldy, T, 2 * I, K, true, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int b200_rms_norm(const void* x, long long x_stride, const void* residual, const void* weight,

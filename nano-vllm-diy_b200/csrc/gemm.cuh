@@ -5,30 +5,38 @@
 // RowParallelLinear.forward, src/layers/llm_head.py:64 ParallelLMHead).
 //
 // Tiling ("swap-AB"): the weight is the M operand (128 output features per
-// CTA) and the tokens are the N operand (BN = 32..256 tokens per CTA), so a
-// decode batch of B <= 256 tokens is a single N tile and every CTA streams a
-// disjoint 128-row slab of W from HBM exactly once.  Both operands are
+// CTA) and the tokens are the N operand (BN = 32..128 tokens per CTA).  The
+// grid runs token tiles fastest, so the CTAs that share a 128-row slab of W
+// are resident together and W is read from HBM once (the siblings hit L2).  Both operands are
 // K-major in global memory (W is [out, in] row-major, X is [T, in]), which is
 // what the tcgen05 K-major shared-memory descriptors want.
+//
+// Two CTAs fit per SM (ring < 110 KB), so one CTA's epilogue overlaps the
+// other's main loop.  Split-K runs inside a thread-block cluster of S CTAs
+// (grid z = S): each CTA reduces a K range into TMEM, stages its fp32 tile in its
+// own shared memory, and after a cluster barrier every CTA sums one slice of
+// the tile's token rows over the S CTAs through distributed shared memory
+// and writes it -- no fp32 workspace in HBM and no separate reduce kernel.
 //
 // Roles (192 threads):
 //   warp 0      TMA producer (one lane): W box 64x128, X box 64xBN, 128-byte
 //               swizzle, into an S-stage ring guarded by full/empty mbarriers
 //   warp 1      TMEM allocator + MMA issuer (one lane): 4 x tcgen05.mma
 //               (M=128, N=BN, K=16) per 64-wide K block, accumulators in TMEM
-//   warps 2..5  epilogue: tcgen05.ld 32x32b -> registers -> global
+//   warps 2..5  TMEM -> shared memory (tcgen05.ld 32x32b), [token][feature]
+//   all warps   cluster reduction + epilogue with 16-byte coalesced stores
 //
 // Epilogues:
-//   EPI_BF16     y = bf16(acc + bias)                       (split == 1)
-//   EPI_F32      ws[split] = acc (fp32 partials, reduced by splitk_reduce)
-//   EPI_SILU     gate/up interleaved tiles: out = bf16(silu(bf16 g) * bf16 u)
+//   EPI_BF16     y = bf16(acc + bias)
+//   EPI_SILU     tiles hold 64 gate rows + the 64 matching up rows of the
+//                [gate ; up] weight; y = bf16(silu(bf16 g) * bf16 u)
 //                (src/layers/activation.py:6-10 fused into the gate_up GEMM)
 #pragma once
 #include "common.cuh"
 
 namespace b200 {
 
-enum GemmEpilogue : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SILU = 2 };
+enum GemmEpilogue : int { EPI_BF16 = 0, EPI_SILU = 2 };
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -40,12 +48,13 @@ struct GemmArgs {
   int BN;              // token tile (multiple of 32, <= 256)
   int stages;          // smem ring depth
   int num_kb;          // ceil(K / 64)
-  int kb_per_split;    // K blocks per split (blockIdx.z)
+  int kb_per_split;    // K blocks per cluster rank
+  int splits;          // cluster size along z
   int tmem_cols;       // power of two >= BN
   int epi;             // GemmEpilogue
-  __nv_bfloat16* y;    // EPI_BF16 / EPI_SILU output
+  int vec_ok;          // y rows are 16-byte aligned: vector stores
+  __nv_bfloat16* y;    // output
   long long ldy;       // row stride of y (elements)
-  float* ws;           // EPI_F32 partials [splits][T][N]
   const __nv_bfloat16* bias;  // [N] or nullptr (EPI_BF16 only)
   int silu_inter;      // EPI_SILU: I (rows of W are [gate(I) ; up(I)])
   unsigned* err;
@@ -73,14 +82,18 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   uint64_t* empty = full + kGemmMaxStages;
   uint64_t* tmem_full = empty + kGemmMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  // after the main loop the ring is reused as the fp32 tile [BN][128]
+  float* s_tile = reinterpret_cast<float*>(smem);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kGemmBM;  // feature tile (EPI_SILU: gate row 64*blockIdx.x)
-  const int t0 = blockIdx.y * p.BN;
+  const int ntile = blockIdx.y;          // feature tile (EPI_SILU: gate rows 64*ntile)
+  const int n0 = ntile * kGemmBM;
+  const int t0 = blockIdx.x * p.BN;
   const int kb0 = blockIdx.z * p.kb_per_split;
   const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
-  const int nk = kb1 - kb0;
+  const int nk = max(0, kb1 - kb0);
+  const int rot = nk > 0 ? (int)((blockIdx.y * 7u + blockIdx.x * 3u) % (unsigned)nk) : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -115,10 +128,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
           break;
         }
         mbar_arrive_expect_tx(&full[s], kABytes + b_bytes);
-        const int kc = (kb0 + i) * kGemmBK;
+        // rotated K order: concurrently running CTAs read different X blocks
+        const int kc = (kb0 + (i + rot) % nk) * kGemmBK;
         if (p.epi == EPI_SILU) {
-          // rows [64 gate | 64 up] of the interleaved tile
-          const int g0 = blockIdx.x * 64;
+          const int g0 = ntile * 64;
           tma_load_2d(a_smem + (size_t)s * kABytes, &tmW, &full[s], kc, g0);
           tma_load_2d(a_smem + (size_t)s * kABytes + kABytes / 2, &tmW, &full[s], kc,
                       p.silu_inter + g0);
@@ -156,66 +169,21 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       mbar_wait(tmem_full, 0, p.err);
     }
   } else {
-    // ---------------- epilogue: warps 2..5 -> TMEM lane quarters 2,3,0,1
+    // ---- TMEM -> shared memory: warps 2..5 own TMEM lane quarters 2,3,0,1
     const int q = warp & 3;
-    const int row = q * 32 + lane;  // accumulator row inside the 128-row tile
+    const int row = q * 32 + lane;  // accumulator row = feature inside the tile
     const bool have = mbar_wait(tmem_full, 0, p.err);
     tc_fence_after();
-    if (p.epi == EPI_SILU) {
-      // lanes 0..63 hold gate rows, 64..127 the matching up rows.  The loop
-      // runs even after a timed-out wait so every epilogue warp reaches the
-      // same named barriers; only the stores are skipped.
-      float* xch = reinterpret_cast<float*>(a_smem);  // 64 x 33 floats
-      const int feat = blockIdx.x * 64 + (row & 63);
-      for (int c = 0; c < p.BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
-        tmem_ld_wait();
-        if (q >= 2) {
+    for (int c = 0; c < p.BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
+      tmem_ld_wait();
+      if (have && nk > 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) xch[(row - 64) * 33 + j] = __uint_as_float(r[j]);
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (have && q < 2 && feat < p.silu_inter) {
+        for (int j = 0; j < 32; ++j) s_tile[(c + j) * kGemmBM + row] = __uint_as_float(r[j]);
+      } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int t = t0 + c + j;
-            if (t < p.T) {
-              const float g = bf16_round(__uint_as_float(r[j]));
-              const float u = bf16_round(xch[row * 33 + j]);
-              p.y[(size_t)t * p.ldy + feat] = __float2bfloat16_rn(silu_mul_ref(g, u));
-            }
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      }
-    } else if (have) {
-      {
-        const int n = n0 + row;
-        float bias_v = 0.f;
-        if (p.epi == EPI_BF16 && p.bias != nullptr && n < p.N) bias_v = __bfloat162float(p.bias[n]);
-        for (int c = 0; c < p.BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)c, r);
-          tmem_ld_wait();
-          if (n < p.N) {
-            if (p.epi == EPI_BF16) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int t = t0 + c + j;
-                if (t < p.T)
-                  p.y[(size_t)t * p.ldy + n] = __float2bfloat16_rn(__uint_as_float(r[j]) + bias_v);
-              }
-            } else {
-              float* dst = p.ws + (size_t)blockIdx.z * p.T * p.N;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int t = t0 + c + j;
-                if (t < p.T) dst[(size_t)t * p.N + n] = __uint_as_float(r[j]);
-              }
-            }
-          }
-        }
+        for (int j = 0; j < 32; ++j) s_tile[(c + j) * kGemmBM + row] = 0.f;
       }
     }
   }
@@ -225,46 +193,76 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     tc_fence_after();
     tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
   }
-}
+  const int splits = p.splits;
+  if (splits > 1) cluster_sync();
 
-// Sum the fp32 split-K partials [splits][T][N] and apply the epilogue.
-//   EPI_BF16: y[t][n] = bf16(sum + bias[n])
-//   EPI_SILU: y[t][j] = silu(bf16 g) * bf16 u with g = col j, u = col j + N/2
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int T, int N,
-                                     __nv_bfloat16* __restrict__ y, long long ldy,
-                                     const __nv_bfloat16* __restrict__ bias, int epi) {
-  const int outN = (epi == EPI_SILU) ? N / 2 : N;
-  const int vecs = outN / 4;
-  const size_t total = (size_t)T * vecs;
-  const size_t plane = (size_t)T * N;
-  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
-       idx += (size_t)gridDim.x * blockDim.x) {
-    const int t = (int)(idx / vecs);
-    const int c = (int)(idx % vecs) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 acc2 = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < splits; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(ws + s * plane + (size_t)t * N + c);
-      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-      if (epi == EPI_SILU) {
-        const float4 u = *reinterpret_cast<const float4*>(ws + s * plane + (size_t)t * N + outN + c);
-        acc2.x += u.x; acc2.y += u.y; acc2.z += u.z; acc2.w += u.w;
+  // ---- reduction over the cluster + epilogue: this CTA's slice of token rows
+  const uint32_t rank = splits > 1 ? cluster_ctarank() : 0u;
+  const int rows_valid = min(p.BN, p.T - t0);
+  const int per = (rows_valid + splits - 1) / splits;
+  const int tb = min(rows_valid, (int)rank * per);
+  const int te = min(rows_valid, tb + per);
+  const uint32_t tile_local = smem_u32(s_tile);
+  auto sum8 = [&](int off_floats, float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    for (int r = 0; r < splits; ++r) {
+      const uint32_t base = splits > 1 ? map_to_rank(tile_local, (uint32_t)r) : tile_local;
+      const uint32_t a = base + (uint32_t)off_floats * 4u;
+      const float4 x0 = ld_dsmem_f4(a);
+      const float4 x1 = ld_dsmem_f4(a + 16);
+      v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+      v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+    }
+  };
+  if (p.epi == EPI_SILU) {
+    // 8 output features (8 gate + the 8 matching up rows) per unit
+    const int units = (te - tb) * 8;
+    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+      const int t = tb + (u >> 3), ch = u & 7;
+      const int feat = ntile * 64 + ch * 8;
+      if (feat >= p.silu_inter) continue;
+      float g[8], up[8], o[8];
+      sum8(t * kGemmBM + ch * 8, g);
+      sum8(t * kGemmBM + 64 + ch * 8, up);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = silu_mul_ref(bf16_round(g[i]), bf16_round(up[i]));
+      __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + feat;
+      if (p.vec_ok && feat + 8 <= p.silu_inter) {
+        uint4 pk;
+        pk.x = pack_bf16x2(o[0], o[1]); pk.y = pack_bf16x2(o[2], o[3]);
+        pk.z = pack_bf16x2(o[4], o[5]); pk.w = pack_bf16x2(o[6], o[7]);
+        *reinterpret_cast<uint4*>(dst) = pk;
+      } else {
+        for (int i = 0; i < 8 && feat + i < p.silu_inter; ++i) dst[i] = __float2bfloat16_rn(o[i]);
       }
     }
-    float o[4] = {acc.x, acc.y, acc.z, acc.w};
-    if (epi == EPI_SILU) {
-      const float u[4] = {acc2.x, acc2.y, acc2.z, acc2.w};
+  } else {
+    const int units = (te - tb) * 16;
+    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+      const int t = tb + (u >> 4), ch = u & 15;
+      const int n = n0 + ch * 8;
+      if (n >= p.N) continue;
+      float v[8];
+      sum8(t * kGemmBM + ch * 8, v);
+      if (p.bias != nullptr) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = silu_mul_ref(bf16_round(o[i]), bf16_round(u[i]));
-    } else if (bias != nullptr) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] += __bfloat162float(bias[c + i]);
+        for (int i = 0; i < 8; ++i)
+          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+      }
+      __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + n;
+      if (p.vec_ok && n + 8 <= p.N) {
+        uint4 pk;
+        pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
+        pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(dst) = pk;
+      } else {
+        for (int i = 0; i < 8 && n + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+      }
     }
-    uint2 packed;
-    packed.x = pack_bf16x2(o[0], o[1]);
-    packed.y = pack_bf16x2(o[2], o[3]);
-    *reinterpret_cast<uint2*>(y + (size_t)t * ldy + c) = packed;
   }
+  // peers may still be reading this CTA's tile
+  if (splits > 1) cluster_sync();
 }
 
 }  // namespace b200

@@ -6,9 +6,10 @@ include/b200ops.h and raises RuntimeError on a non-zero status.  There is no
 fallback: if the shared library is missing or a tensor is not on a CUDA
 device, the call fails.
 
-Workspaces (split-K partials of the GEMMs, split-KV partials of decode
-attention) are per-device torch buffers that grow on demand outside CUDA-graph
-capture and are reused by every call.
+The decode-attention workspace (split-KV partials and its scheduling
+tickets) is a per-device torch buffer that grows on demand outside CUDA-graph
+capture and is reused by every call; the GEMMs need none (split-K partials
+are reduced in cluster shared memory).
 """
 from __future__ import annotations
 
@@ -143,7 +144,6 @@ def reserve_workspace(kind: str, nbytes: int, device: torch.device) -> None:
     workspace(kind, nbytes, device)
 
 
-GEMM_WS_DEFAULT = 64 << 20
 
 
 def launch_count() -> int:
@@ -179,9 +179,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     y2 = out.view(-1, N)
     if w.stride(-1) != 1:
         raise ValueError("linear: weight rows must be contiguous")
-    ws = workspace("gemm", GEMM_WS_DEFAULT, x.device)
     _check(lib.b200_linear(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(bias), _p(y2), y2.stride(0),
-                           T, N, K, _p(ws), ws.numel(), _stream()), "b200_linear")
+                           T, N, K, None, 0, _stream()), "b200_linear")
     return out
 
 
@@ -196,12 +195,19 @@ def linear_silu_and_mul(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | No
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
     T = x2.shape[0]
+    if I % 64:
+        # the fused epilogue pairs 64-row gate / up blocks; other widths run
+        # the GEMM and the activation as two kernels
+        act = silu_and_mul(linear(x2, w))
+        if out is None:
+            return act.view(*x.shape[:-1], I)
+        out.view(-1, I).copy_(act)
+        return out
     if out is None:
         out = torch.empty(*x.shape[:-1], I, dtype=x.dtype, device=x.device)
     y2 = out.view(-1, I)
-    ws = workspace("gemm", GEMM_WS_DEFAULT, x.device)
     _check(lib.b200_linear_silu_and_mul(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(y2),
-                                        y2.stride(0), T, I, K, _p(ws), ws.numel(), _stream()),
+                                        y2.stride(0), T, I, K, None, 0, _stream()),
            "b200_linear_silu_and_mul")
     return out
 

@@ -92,7 +92,6 @@ class ModelRunner:
         self.num_kvcache_blocks = num_blocks
         nbytes = b200.attention_workspace_bytes(self.max_num_seqs, self.max_seq_len, self.local_q_heads)
         b200.reserve_workspace("attn", nbytes, self.device)
-        b200.reserve_workspace("gemm", b200.GEMM_WS_DEFAULT, self.device)
 
     # ------------------------------------------------------------------ steps
     def prepare(self, seqs) -> tuple[torch.Tensor, torch.Tensor, Context]:
