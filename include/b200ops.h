@@ -168,6 +168,33 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
                          float softmax_scale, void* out, long long out_stride, void* workspace,
                          size_t ws_bytes, b200_stream_t stream);
 
+/* Allocation-free variant of the decode path of b200_paged_attention (every
+ * sequence has query length 1, K/V from the paged cache): the same kernel,
+ * with its scratch in a fixed 32 MiB array inside the library instead of a
+ * caller workspace.  No counterpart in the reference: it is for callers that
+ * cannot allocate device memory -- hosts that reach this library through a
+ * foreign-function boundary with device memory owned elsewhere, or serving
+ * loops that must not call cudaMalloc (it may synchronise the device and
+ * cannot be recorded into a CUDA graph).
+ *  - Limits: B <= 1024, Hkv <= 64, Hq / Hkv <= 8, page a multiple of 256, and
+ *    256 KiB + B * ceil(max_seqlen_k / 256) * Hq * 520 bytes must fit the
+ *    32 MiB array (e.g. 128 sequences of 4096 keys with 32 heads); larger
+ *    problems return B200_ERR_WORKSPACE without launching anything.
+ *  - The first call on a device looks up the array's device address; make
+ *    that first call before any CUDA-graph capture.
+ *  - Every call clears the array's counters on `stream` and then uses it, so
+ *    calls on different streams that overlap on the GPU race with each
+ *    other; serialise them.
+ *  - Allocates nothing (no cudaMalloc / cudaFree); the array stays resident on
+ *    every GPU that loaded the library until the process exits. */
+int b200_paged_decode_attention_static(const void* q, long long q_stride, int num_q_rows,
+                                       const void* k_cache, const void* v_cache,
+                                       long long num_slots, const int* block_tables,
+                                       int bt_stride, int bt_width, const int* cu_seqlens_q,
+                                       const int* cu_seqlens_k, int B, int max_seqlen_k, int Hq,
+                                       int Hkv, int page, float softmax_scale, void* out,
+                                       long long out_stride, b200_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Vocabulary
  * ------------------------------------------------------------------------ */

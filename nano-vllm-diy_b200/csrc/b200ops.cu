@@ -522,3 +522,105 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Allocation-free decode attention
+//
+// Some callers cannot hand this library a workspace: a host runtime that
+// reaches these kernels through a foreign-function boundary (cgo, JNI,
+// ctypes) with device memory owned by another allocator, or a serving loop
+// that must never call cudaMalloc -- cudaMalloc can synchronise the device
+// and stall every stream, and it cannot be recorded into a CUDA graph.  For
+// them b200_paged_decode_attention_static keeps the decode kernel's scratch
+// (per-(sequence, kv head) tickets, the work counter and the split-KV
+// partials) in the fixed array below.  The array is part of the library
+// image: every GPU that loads libb200ops.so holds these 32 MiB until the
+// process exits.
+// ===========================================================================
+namespace {
+
+constexpr size_t kStaticDecodeScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) unsigned char g_static_decode_scratch[kStaticDecodeScratchBytes];
+
+// Device address of the array on the current device, looked up once per
+// device (host code may not use the symbol itself as a device pointer).
+int static_decode_scratch(void** out) {
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(B200_ERR_INVALID, "device %d out of range", dev);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_decode_scratch);
+    if (e != cudaSuccess)
+      return fail(B200_ERR_CUDA, "scratch symbol address: %s", cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return B200_OK;
+}
+
+}  // namespace
+
+extern "C" int b200_paged_decode_attention_static(
+    const void* q, long long q_stride, int num_q_rows, const void* k_cache, const void* v_cache,
+    long long num_slots, const int* block_tables, int bt_stride, int bt_width,
+    const int* cu_seqlens_q, const int* cu_seqlens_k, int B, int max_seqlen_k, int Hq, int Hkv,
+    int page, float softmax_scale, void* out, long long out_stride, b200_stream_t stream) {
+  if (B <= 0) return B200_OK;
+  if (Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq / Hkv > 8 || Hkv > kDecMaxKvHeads || B > kDecMaxSeqs)
+    return fail(B200_ERR_UNSUPPORTED,
+                "decode_static: needs Hq %% Hkv == 0, Hq/Hkv <= 8, Hkv <= %d, B <= %d", kDecMaxKvHeads,
+                kDecMaxSeqs);
+  if (!q || !k_cache || !v_cache || !block_tables || !cu_seqlens_q || !cu_seqlens_k || !out ||
+      page <= 0 || page % kDecItem || num_q_rows <= 0 || max_seqlen_k < 0)
+    return fail(B200_ERR_INVALID, "decode_static: missing argument or page not a multiple of %d", kDecItem);
+  if (q_stride % 8 || out_stride % 8 || !aligned16(q) || !aligned16(out) || !aligned16(k_cache) ||
+      !aligned16(v_cache))
+    return fail(B200_ERR_INVALID, "decode_static: rows must be 16-byte aligned");
+  const size_t per_item = (size_t)Hq * (kDecHD + 2) * sizeof(float);
+  const size_t items = (size_t)B * ((max_seqlen_k + kDecItem - 1) / kDecItem);
+  const size_t need = (size_t)kDecTicketBytes + items * per_item;
+  if (need > kStaticDecodeScratchBytes)
+    return fail(B200_ERR_WORKSPACE,
+                "decode_static: %d sequences of up to %d keys with %d heads need %zu bytes of scratch; "
+                "the fixed array holds %zu",
+                B, max_seqlen_k, Hq, need, kStaticDecodeScratchBytes);
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  void* scratch = nullptr;
+  if (int r = static_decode_scratch(&scratch)) return r;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // the tickets and the work counter must start at zero; a call that ended
+  // early must not leave stale counts for this one
+  cudaError_t e = cudaMemsetAsync(scratch, 0, kDecTicketBytes, st);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "decode_static: clear: %s", cudaGetErrorString(e));
+  CUtensorMap tmK, tmV, tmQ;
+  const int qbox = Hq < 8 ? Hq : 8;
+  if (int r = make_tmap_3d(&tmK, k_cache, kDecHD, Hkv, (uint64_t)num_slots, kDecHD * 2,
+                           (uint64_t)Hkv * kDecHD * 2, 64, 1, kDecTile))
+    return r;
+  if (int r = make_tmap_3d(&tmV, v_cache, kDecHD, Hkv, (uint64_t)num_slots, kDecHD * 2,
+                           (uint64_t)Hkv * kDecHD * 2, 64, 1, kDecTile))
+    return r;
+  if (int r = make_tmap_3d(&tmQ, q, kDecHD, Hq, (uint64_t)num_q_rows, kDecHD * 2,
+                           (uint64_t)q_stride * 2, 64, (uint32_t)qbox, 1))
+    return r;
+  DecodeArgs a{};
+  a.block_tables = block_tables; a.bt_stride = bt_stride; a.bt_width = bt_width;
+  a.cu_q = cu_seqlens_q; a.cu_k = cu_seqlens_k;
+  a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = Hq / Hkv; a.page = page; a.q_box_rows = qbox;
+  a.num_slots = num_slots;
+  a.scale_log2 = softmax_scale * 1.4426950408889634f;
+  a.tickets = static_cast<int*>(scratch);
+  a.cap_items = (long long)((kStaticDecodeScratchBytes - kDecTicketBytes) / per_item);
+  a.part_ml = reinterpret_cast<float*>(static_cast<char*>(scratch) + kDecTicketBytes);
+  a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
+  a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
+  a.err = ds->err;
+  const int smem = dec_smem_bytes();
+  if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
+  decode_attn_kernel<<<ds->num_sms, kDecWarps * 32, smem, st>>>(tmK, tmV, tmQ, a);
+  return check_launch("decode_attn_kernel");
+}

@@ -51,6 +51,9 @@ _SIGNATURES = {
     "b200_embedding": ([_c_void_p, _c_void_p, _c_void_p, _i, _i, _ll, _ll, _c_void_p], _i),
     "b200_argmax": ([_c_void_p, _ll, _i, _i, _c_void_p, _c_void_p], _i),
     "b200_attention_workspace_bytes": ([_i, _i, _i, ctypes.POINTER(_sz)], _i),
+    "b200_paged_decode_attention_static": ([_c_void_p, _ll, _i, _c_void_p, _c_void_p, _ll,
+                                            _c_void_p, _i, _i, _c_void_p, _c_void_p, _i, _i,
+                                            _i, _i, _i, _f, _c_void_p, _ll, _c_void_p], _i),
     "b200_paged_attention": ([_c_void_p, _ll, _i, _c_void_p, _ll, _c_void_p, _ll, _c_void_p,
                               _c_void_p, _ll, _c_void_p, _i, _i, _c_void_p, _c_void_p, _i, _i, _i,
                               _i, _i, _i, _f, _c_void_p, _ll, _c_void_p, _sz, _c_void_p], _i),
