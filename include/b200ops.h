@@ -84,6 +84,36 @@ int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long l
                              long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
                              b200_stream_t stream);
 
+/* RowParallelLinear at tp > 1 in one launch: y = sum over ranks of
+ * bf16(x_r * w_r^T (+ bias on rank 0)), the all-reduce of
+ * src/layers/linear.py:169-173 (torch.distributed.all_reduce after F.linear)
+ * fused into the GEMM epilogue over NVLink peer memory.  Every rank calls it
+ * with the same shapes; stage / out / flags / done are arrays of `world`
+ * device pointers giving each rank's address of its symmetric buffers
+ * (rank r's own entry at index r):
+ *   stage[r]: bf16 [world][stage_rows][ldo]   partials received by rank r
+ *   out[r]:   bf16 [stage_rows][ldo]          reduced output on rank r
+ *   flags[r], done[r]: uint32 [max_positions], zero before the first call
+ *                       (every call leaves them zero)
+ * The reduced y is in out[rank] (rows [0, T), columns [0, N)) when the
+ * launch completes on this rank's stream.  Returns B200_ERR_UNSUPPORTED
+ * without launching when the CTAs of the launch could not all be resident
+ * at once (the owner ranks wait on peer CTAs) or the sizes exceed the
+ * buffers; the caller then runs b200_linear + a collective.  Waits on peer
+ * flags are bounded (1 s) and set B200_DEVERR_PEER_TIMEOUT. */
+int b200_linear_allreduce(const void* x, long long ldx, const void* w, long long ldw,
+                          const void* bias, int T, int N, int K, int rank, int world,
+                          void* const* stage, void* const* out, void* const* flags,
+                          void* const* done, long long stage_rows, long long ldo,
+                          long long max_positions, b200_stream_t stream);
+
+/* CUDA IPC helpers for the symmetric buffers: export the allocation that
+ * holds `ptr` (64-byte handle + offset of ptr inside it), map a peer's
+ * export into this process, and unmap it. */
+int b200_ipc_export(const void* ptr, void* handle, unsigned long long* offset);
+int b200_ipc_import(const void* handle, unsigned long long offset, void** ptr);
+int b200_ipc_close(void* ptr, unsigned long long offset);
+
 /* ------------------------------------------------------------------------
  * Normalisation, RoPE, activation
  * ------------------------------------------------------------------------ */

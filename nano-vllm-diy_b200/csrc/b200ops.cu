@@ -85,14 +85,20 @@ int device_state(DeviceState** out) {
   return B200_OK;
 }
 
+// Raise a kernel's dynamic shared-memory limit to at least `bytes` (once per
+// kernel, device and size; the limit must leave room for static smem).
 template <typename K>
 int ensure_smem(DeviceState* ds, unsigned bit, K kernel, int bytes) {
-  if (ds->smem_configured & bit) return B200_OK;
-  const cudaError_t e =
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "smem attribute: %s", cudaGetErrorString(e));
-  (void)bytes;
-  ds->smem_configured |= bit;
+  static int configured[kMaxDevices][8] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int slot = 0;
+  while ((1u << slot) != bit && slot < 7) ++slot;
+  if (configured[dev][slot] >= bytes) return B200_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "smem attribute (%d bytes): %s", bytes, cudaGetErrorString(e));
+  configured[dev][slot] = bytes;
+  (void)ds;
   return B200_OK;
 }
 
@@ -105,6 +111,19 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
                                          &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 3020, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
   }
   return fn;
 }
@@ -254,6 +273,99 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tn_tcgen05_kernel, tmW, tmX, a);
   if (e != cudaSuccess) return fail(B200_ERR_CUDA, "gemm launch: %s", cudaGetErrorString(e));
   return check_launch("gemm_tn_tcgen05_kernel");
+}
+
+// Fused RowParallelLinear: GEMM + all-reduce in one launch (EPI_ALLREDUCE).
+int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
+                       int T, int N, int K, const AllReducePeers& ar, long long max_positions,
+                       cudaStream_t st) {
+  if (T <= 0) return B200_OK;
+  if (N <= 0 || K <= 0 || N % 8) return fail(B200_ERR_INVALID, "linear_allreduce: N=%d must be a multiple of 8", N);
+  if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K)
+    return fail(B200_ERR_INVALID, "linear_allreduce: K and row strides must be multiples of 8");
+  if (!aligned16(x) || !aligned16(w)) return fail(B200_ERR_INVALID, "linear_allreduce: x and w must be 16-byte aligned");
+  if (ar.world < 1 || ar.world > kMaxTpRanks || ar.rank < 0 || ar.rank >= ar.world)
+    return fail(B200_ERR_INVALID, "linear_allreduce: rank %d / world %d", ar.rank, ar.world);
+  if (T > ar.stage_rows || ar.ldo < N || ar.ldo % 8)
+    return fail(B200_ERR_UNSUPPORTED, "linear_allreduce: %d rows exceed the %lld staged rows (or ldo)", T, ar.stage_rows);
+  for (int r = 0; r < ar.world; ++r)
+    if (!ar.stage[r] || !ar.out[r] || !ar.flags[r] || !ar.done[r] || !aligned16(ar.stage[r]) ||
+        !aligned16(ar.out[r]))
+      return fail(B200_ERR_PEER, "linear_allreduce: peer buffers of rank %d are missing", r);
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  GemmPlan p = plan_gemm(ds, T, N, K, false);
+  if (int r = ensure_smem(ds, 1u, gemm_tn_tcgen05_kernel, p.smem)) return r;
+  // every CTA must be resident at once (owners wait for peers' CTAs): take the
+  // largest K split, down to none, whose grid fits the co-resident slots
+  auto resident_for = [&](int splits) -> long long {
+    if (splits == 1) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_tn_tcgen05_kernel, kGemmThreads,
+                                                        p.smem) != cudaSuccess) {
+        cudaGetLastError();
+        per_sm = 0;
+      }
+      return (long long)per_sm * ds->num_sms;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, splits);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = p.smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = splits;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tn_tcgen05_kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      clusters = 0;
+    }
+    return (long long)clusters * splits;
+  };
+  const long long tiles = (long long)p.n_tiles * p.token_tiles;
+  int splits = p.splits;
+  while (splits > 1 && tiles * splits > resident_for(splits)) --splits;
+  if (splits != p.splits) {
+    p.kb_per_split = (p.num_kb + splits - 1) / splits;
+    p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  }
+  const long long ctas = tiles * p.splits;
+  if (ctas > max_positions)
+    return fail(B200_ERR_UNSUPPORTED, "linear_allreduce: %lld CTA positions exceed the %lld flags", ctas, max_positions);
+  const long long resident = resident_for(p.splits);
+  if (ctas > resident)
+    return fail(B200_ERR_UNSUPPORTED, "linear_allreduce: %lld CTAs cannot all be resident (%lld)", ctas, resident);
+  CUtensorMap tmW, tmX;
+  if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK, (uint32_t)kGemmBM)) return r;
+  if (int r = make_tmap(&tmX, x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx, kGemmBK, (uint32_t)p.BN)) return r;
+  GemmArgs a{};
+  a.T = T; a.N = N; a.K = K; a.BN = p.BN; a.stages = p.stages; a.num_kb = p.num_kb;
+  a.kb_per_split = p.kb_per_split; a.splits = p.splits; a.tmem_cols = p.tmem_cols;
+  a.epi = EPI_ALLREDUCE;
+  a.vec_ok = 1;
+  a.y = nullptr; a.ldy = ar.ldo;
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.err = ds->err;
+  a.ar = ar;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.token_tiles, p.n_tiles, p.splits);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = p.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.splits > 1 ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tn_tcgen05_kernel, tmW, tmX, a);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "gemm allreduce launch: %s", cudaGetErrorString(e));
+  return check_launch("gemm_tn_tcgen05_kernel(allreduce)");
 }
 
 }  // namespace
@@ -519,6 +631,62 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
   dim3 grid((max_seqlen_q + kPfBM - 1) / kPfBM, Hq, B);
   prefill_attn_kernel<<<grid, 128, smem, st>>>(a);
   return check_launch("prefill_attn_kernel");
+}
+
+int b200_ipc_export(const void* ptr, void* handle, unsigned long long* offset) {
+  if (!ptr || !handle || !offset) return fail(B200_ERR_INVALID, "ipc_export: null argument");
+  auto range = address_range_fn();
+  if (!range) return fail(B200_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(B200_ERR_CUDA, "ipc_export: pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof(h));
+  *offset = (unsigned long long)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return B200_OK;
+}
+
+int b200_ipc_import(const void* handle, unsigned long long offset, void** ptr) {
+  if (!handle || !ptr) return fail(B200_ERR_INVALID, "ipc_import: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  *ptr = static_cast<char*>(base) + offset;
+  return B200_OK;
+}
+
+int b200_ipc_close(void* ptr, unsigned long long offset) {
+  if (!ptr) return B200_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return B200_OK;
+}
+
+int b200_linear_allreduce(const void* x, long long ldx, const void* w, long long ldw,
+                          const void* bias, int T, int N, int K, int rank, int world,
+                          void* const* stage, void* const* out, void* const* flags,
+                          void* const* done, long long stage_rows, long long ldo,
+                          long long max_positions, b200_stream_t stream) {
+  if (world < 1 || world > kMaxTpRanks || !stage || !out || !flags || !done)
+    return fail(B200_ERR_INVALID, "linear_allreduce: world %d / peer arrays", world);
+  AllReducePeers ar{};
+  ar.rank = rank;
+  ar.world = world;
+  ar.stage_rows = stage_rows;
+  ar.ldo = ldo;
+  for (int r = 0; r < world; ++r) {
+    ar.stage[r] = static_cast<__nv_bfloat16*>(stage[r]);
+    ar.out[r] = static_cast<__nv_bfloat16*>(out[r]);
+    ar.flags[r] = static_cast<unsigned*>(flags[r]);
+    ar.done[r] = static_cast<unsigned*>(done[r]);
+  }
+  return run_gemm_allreduce(x, ldx, w, ldw, bias, T, N, K, ar, max_positions,
+                            reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

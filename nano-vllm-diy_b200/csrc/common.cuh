@@ -109,7 +109,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, no multicast)
+// TMA (tiled loads into this CTA's own shared memory)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

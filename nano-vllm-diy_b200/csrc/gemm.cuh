@@ -28,6 +28,11 @@
 //
 // Epilogues:
 //   EPI_BF16     y = bf16(acc + bias)
+//   EPI_ALLREDUCE  RowParallelLinear at tp > 1: the bf16 partial of every
+//                CTA position goes by NVLink peer stores to the position's
+//                owner rank, which sums the world's partials in fp32 (fixed
+//                rank order) and stores the bf16 result into every rank's
+//                output buffer; flag handshakes are bounded waits
 //   EPI_SILU     tiles hold 64 gate rows + the 64 matching up rows of the
 //                [gate ; up] weight; y = bf16(silu(bf16 g) * bf16 u)
 //                (src/layers/activation.py:6-10 fused into the gate_up GEMM)
@@ -36,7 +41,20 @@
 
 namespace b200 {
 
-enum GemmEpilogue : int { EPI_BF16 = 0, EPI_SILU = 2 };
+enum GemmEpilogue : int { EPI_BF16 = 0, EPI_SILU = 2, EPI_ALLREDUCE = 3 };
+
+constexpr int kMaxTpRanks = 8;
+
+// Symmetric buffers of the fused GEMM + all-reduce (EPI_ALLREDUCE); index r
+// holds rank r's address of each buffer (this rank's own entry included).
+struct AllReducePeers {
+  __nv_bfloat16* stage[kMaxTpRanks];  // [world][stage_rows][ldo] partial products
+  __nv_bfloat16* out[kMaxTpRanks];    // [stage_rows][ldo] reduced output
+  unsigned* flags[kMaxTpRanks];       // per CTA position: partials received (owner side)
+  unsigned* done[kMaxTpRanks];        // per CTA position: reduced rows written (every rank)
+  int rank, world;
+  long long stage_rows, ldo;
+};
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
@@ -58,7 +76,31 @@ struct GemmArgs {
   const __nv_bfloat16* bias;  // [N] or nullptr (EPI_BF16 only)
   int silu_inter;      // EPI_SILU: I (rows of W are [gate(I) ; up(I)])
   unsigned* err;
+  AllReducePeers ar;   // EPI_ALLREDUCE only
 };
+
+// System-scope flag helpers for the cross-GPU handshake.
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *p == want; resets *p to 0 afterwards (the flag is
+// consumed).  Returns false and records ERR_PEER_TIMEOUT after 1 s.
+__device__ __forceinline__ bool wait_flag_and_reset(unsigned* p, unsigned want, unsigned* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_sys(p) < want) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_error(err, ERR_PEER_TIMEOUT);
+      return false;
+    }
+  }
+  atomicExch(p, 0u);
+  return true;
+}
 
 __device__ __forceinline__ float silu_mul_ref(float g, float u) {
   // F.silu on a bf16 tensor rounds its result to bf16, the product rounds
@@ -236,6 +278,79 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       } else {
         for (int i = 0; i < 8 && feat + i < p.silu_inter; ++i) dst[i] = __float2bfloat16_rn(o[i]);
       }
+    }
+  } else if (p.epi == EPI_ALLREDUCE) {
+    // ---- fused all-reduce over NVLink peer memory (RowParallelLinear at tp > 1,
+    // src/layers/linear.py:169-173).  Position = (token tile, feature tile,
+    // cluster rank); its owner rank sums the world's partials.
+    const AllReducePeers& ar = p.ar;
+    const unsigned pos = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    const int owner = (int)(pos % (unsigned)ar.world);
+    const int units = (te - tb) * 16;
+    __nv_bfloat16* stage_dst = ar.stage[owner] + (size_t)ar.rank * ar.stage_rows * ar.ldo;
+    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+      const int t = tb + (u >> 4), ch = u & 15;
+      const int n = n0 + ch * 8;
+      if (n >= p.N) continue;
+      float v[8];
+      sum8(t * kGemmBM + ch * 8, v);
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+      }
+      // this rank's partial, rounded to bf16 as F.linear's output is
+      uint4 pk;
+      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
+      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4*>(stage_dst + (size_t)(t0 + t) * ar.ldo + n) = pk;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      red_release_sys_add(ar.flags[owner] + pos, 1u);
+    }
+    if (owner == ar.rank) {
+      __shared__ int s_ok;
+      if (threadIdx.x == 0) s_ok = wait_flag_and_reset(ar.flags[ar.rank] + pos, (unsigned)ar.world, p.err);
+      __syncthreads();
+      if (s_ok) {
+        for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+          const int t = tb + (u >> 4), ch = u & 15;
+          const int n = n0 + ch * 8;
+          if (n >= p.N) continue;
+          float acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+          for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
+            const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
+                ar.stage[ar.rank] + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
+            const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = unpack_bf16x2(qw[k]);
+              acc[2 * k] += f.x;
+              acc[2 * k + 1] += f.y;
+            }
+          }
+          uint4 pk;
+          pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
+          pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
+          for (int r = 0; r < ar.world; ++r)
+            *reinterpret_cast<uint4*>(ar.out[r] + (size_t)(t0 + t) * ar.ldo + n) = pk;
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < ar.world; ++r)
+          if (r != ar.rank) red_release_sys_add(ar.done[r] + pos, 1u);
+      }
+    } else {
+      // the owner writes this rank's copy of the reduced rows; wait for it so
+      // that the kernel's completion means the output is complete here
+      if (threadIdx.x == 0) wait_flag_and_reset(ar.done[ar.rank] + pos, 1u, p.err);
+      __syncthreads();
     }
   } else {
     const int units = (te - tb) * 16;

@@ -39,6 +39,12 @@ _SIGNATURES = {
                      _c_void_p, _sz, _c_void_p], _i),
     "b200_linear_silu_and_mul": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _ll, _i, _i, _i,
                                   _c_void_p, _sz, _c_void_p], _i),
+    "b200_linear_allreduce": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _i, _i, _i, _i, _i,
+                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _ll, _ll, _ll,
+                               _c_void_p], _i),
+    "b200_ipc_export": ([_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_ulonglong)], _i),
+    "b200_ipc_import": ([_c_void_p, ctypes.c_ulonglong, ctypes.POINTER(_c_void_p)], _i),
+    "b200_ipc_close": ([_c_void_p, ctypes.c_ulonglong], _i),
     "b200_rms_norm": ([_c_void_p, _ll, _c_void_p, _c_void_p, _c_void_p, _ll, _c_void_p, _i, _i,
                        _f, _c_void_p], _i),
     "b200_qk_norm_rope_store": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _ll, _i, _i, _i,
@@ -213,6 +219,49 @@ def linear_silu_and_mul(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | No
                                         y2.stride(0), T, I, K, None, 0, _stream()),
            "b200_linear_silu_and_mul")
     return out
+
+
+ERR_UNSUPPORTED = -2
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding t, offset of t in it)."""
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_ulonglong(0)
+    _check(load_library().b200_ipc_export(_p(t), h, ctypes.byref(off)), "b200_ipc_export")
+    return h.raw, off.value
+
+
+def ipc_import(handle: bytes, offset: int) -> int:
+    """Device address, in this process, of a peer's exported buffer."""
+    ptr = ctypes.c_void_p()
+    _check(load_library().b200_ipc_import(handle, offset, ctypes.byref(ptr)), "b200_ipc_import")
+    return ptr.value
+
+
+def ipc_close(ptr: int, offset: int) -> None:
+    _check(load_library().b200_ipc_close(ctypes.c_void_p(ptr), offset), "b200_ipc_close")
+
+
+def linear_allreduce(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, rank: int,
+                     world: int, stage: list[int], out: list[int], flags: list[int],
+                     done: list[int], stage_rows: int, ldo: int, max_positions: int) -> int:
+    """Fused GEMM + all-reduce; returns the C status (0, or ERR_UNSUPPORTED when
+    the caller must fall back) and raises on any other failure."""
+    lib = load_library()
+    _cuda(x, w, bias)
+    _bf16(x, w, bias)
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    arr = ctypes.c_void_p * world
+    rc = lib.b200_linear_allreduce(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(bias), x2.shape[0],
+                                   w.shape[0], K, rank, world, arr(*stage), arr(*out), arr(*flags),
+                                   arr(*done), stage_rows, ldo, max_positions, _stream())
+    if rc not in (0, ERR_UNSUPPORTED):
+        _check(rc, "b200_linear_allreduce")
+    return rc
 
 
 # ---------------------------------------------------------------------------

@@ -1,0 +1,112 @@
+"""Fused RowParallelLinear (GEMM + all-reduce over NVLink) for tp > 1.
+
+The reference computes y_r = F.linear(x_r, W_r) on every rank and sums with
+torch.distributed.all_reduce (src/layers/linear.py:169-173).  Here one kernel
+per rank does both: each CTA's bf16 partial goes by peer stores to the rank
+that owns that part of the output, the owner sums the world's partials in a
+fixed rank order and writes the result into every rank's output buffer
+(libb200ops: b200_linear_allreduce).
+
+Symmetric memory: every rank allocates one device buffer holding
+  stage  bf16 [world][max_tokens][ldo]   partials this rank owns
+  out    bf16 [2][max_tokens][ldo]       reduced outputs (ping-pong)
+  flags, done  uint32 [MAX_POSITIONS]    handshake counters (start at zero)
+and exchanges its CUDA IPC handle through the default process group (after
+init_process_group, outside graph capture), so every rank knows every
+rank's address of each part.
+
+The returned tensor is a view of an output buffer that the call after the
+next one overwrites (two buffers alternate), which is how the decoder
+consumes it (the next RMSNorm reads it before the next row-parallel layer).
+Batches that the fused kernel does not take (more than max_tokens rows, or
+a launch whose CTAs could not all be resident) fall back to GEMM +
+torch.distributed.all_reduce on every rank alike.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from src import b200
+
+MAX_POSITIONS = 4096
+
+
+class FusedRowParallel:
+
+    def __init__(self, device: torch.device, max_tokens: int = 512, max_hidden: int = 8192,
+                 group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the fused all-reduce supports up to 8 ranks")
+        self.device = device
+        self.max_tokens = max_tokens
+        self.ldo = (max_hidden + 7) // 8 * 8
+        elt = 2
+        self.stage_bytes = self.world * max_tokens * self.ldo * elt
+        self.out_bytes = max_tokens * self.ldo * elt
+        flag_bytes = MAX_POSITIONS * 4
+        self.off_stage = 0
+        self.off_out = [self.stage_bytes, self.stage_bytes + self.out_bytes]
+        self.off_flags = self.stage_bytes + 2 * self.out_bytes
+        self.off_done = self.off_flags + flag_bytes
+        total = self.off_done + flag_bytes
+        self.buf = torch.zeros(total, dtype=torch.uint8, device=device)
+        handle, offset = b200.ipc_export(self.buf)
+        gathered = [None] * self.world
+        dist.all_gather_object(gathered, (handle, offset), group=group)
+        self.bases: list[int] = []
+        self._opened: list[tuple[int, int]] = []
+        for r, (h, off) in enumerate(gathered):
+            if r == self.rank:
+                self.bases.append(self.buf.data_ptr())
+            else:
+                ptr = b200.ipc_import(h, off)
+                self._opened.append((ptr, off))
+                self.bases.append(ptr)
+        self.outs = [self.buf[o:o + self.out_bytes].view(torch.bfloat16).view(max_tokens, self.ldo)
+                     for o in self.off_out]
+        self._flip = 0
+        self.fused_calls = 0
+        self.fallback_calls = 0
+        self.fallback_reason = ""
+        dist.barrier(group=group)
+
+    @classmethod
+    def create(cls, device: torch.device, max_tokens: int = 512, max_hidden: int = 8192):
+        return cls(device, max_tokens, max_hidden)
+
+    def _addrs(self, off: int) -> list[int]:
+        return [b + off for b in self.bases]
+
+    def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor,
+                         bias: torch.Tensor | None = None) -> torch.Tensor:
+        T = x.reshape(-1, x.shape[-1]).shape[0]
+        N = w.shape[0]
+        if T <= self.max_tokens and N <= self.ldo:
+            idx = self._flip
+            rc = b200.linear_allreduce(
+                x, w, bias, self.rank, self.world, self._addrs(self.off_stage),
+                self._addrs(self.off_out[idx]), self._addrs(self.off_flags),
+                self._addrs(self.off_done), self.max_tokens, self.ldo, MAX_POSITIONS)
+            if rc == 0:
+                self._flip ^= 1
+                self.fused_calls += 1
+                return self.outs[idx][:T, :N].view(*x.shape[:-1], N)
+        self.fallback_calls += 1
+        self.fallback_reason = b200.load_library().b200_last_error().decode(errors="replace")
+        y = b200.linear(x, w, bias)
+        dist.all_reduce(y, group=self.group)
+        return y
+
+    def close(self) -> None:
+        if self.buf is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for ptr, off in self._opened:
+            b200.ipc_close(ptr, off)
+        self._opened.clear()
+        self.buf = None

@@ -1,0 +1,150 @@
+"""Tensor parallelism on 2 GPUs (NCCL process group, one process per GPU).
+
+* the fused RowParallelLinear (GEMM + all-reduce over NVLink peer memory)
+  against the oracle's restatement of src/layers/linear.py:169-173 --
+  sum over ranks of each rank's bf16 partial product, rounded once;
+  every rank must hold the bit-identical result;
+* fifty calls in a row (the handshake flags reset themselves);
+* the Qwen3 model at tp = 2 against the oracle's tp = 2 forward.
+
+Skipped unless the machine shows at least two GPUs.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _init(rank, world, port):
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    return torch.device("cuda", rank)
+
+
+def _fused_worker(rank, world, port):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "nano-vllm-diy_b200")]
+    import torch.distributed as dist
+    from oracle import layers as L
+    from src import b200
+    from src.layers.tp_allreduce import FusedRowParallel
+    dev = _init(rank, world, port)
+    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=4096)
+    try:
+        N, K = 4096, 2048
+        for T in (1, 7, 64, 256, 300, 512):
+            gen = torch.Generator().manual_seed(T)
+            x = torch.randn(T, K, generator=gen).to(torch.bfloat16)
+            w = (torch.randn(N, K, generator=gen) * 0.02).to(torch.bfloat16)
+            xs, ws = x.chunk(world, -1), w.chunk(world, 1)
+            ref = sum(L.linear(xs[r], ws[r]).float() for r in range(world)).to(torch.bfloat16)
+            y = comm.linear_allreduce(xs[rank].contiguous().to(dev), ws[rank].contiguous().to(dev))
+            torch.cuda.synchronize()
+            assert comm.fallback_calls == 0, f"fused path not taken (T={T}): {comm.fallback_reason}"
+            err = L.rel_err(y.cpu(), ref)
+            assert err <= 1e-2, (T, err)
+            parts = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(parts, y.contiguous())
+            for p in parts:
+                assert torch.equal(p, parts[0]), "ranks disagree"
+        # fifty calls in a row on one shape
+        gen = torch.Generator().manual_seed(99)
+        x = torch.randn(256, K, generator=gen).to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=gen) * 0.02).to(torch.bfloat16)
+        xd, wd = x.chunk(world, -1)[rank].contiguous().to(dev), w.chunk(world, 1)[rank].contiguous().to(dev)
+        first = comm.linear_allreduce(xd, wd).clone()
+        for _ in range(50):
+            y = comm.linear_allreduce(xd, wd)
+        torch.cuda.synchronize()
+        assert torch.equal(y, first)
+        assert b200.device_error(clear=True) == 0
+    finally:
+        comm.close()
+        dist.destroy_process_group()
+
+
+def _model_worker(rank, world, port):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "nano-vllm-diy_b200")]
+    import torch.distributed as dist
+    from oracle import layers as L
+    from oracle import model as OM
+    from oracle.metadata import SeqState, prepare_seqs
+    from oracle.weights import Qwen3Shape, random_weights
+    from src import b200
+    from src.engine.model_runner import ModelRunner
+    from src.layers import tp_comm
+    from src.layers.pos_embedding import _table_cpu
+    from src.layers.tp_allreduce import FusedRowParallel
+    dev = _init(rank, world, port)
+    tp_comm.set_comm(FusedRowParallel(dev, max_tokens=512, max_hidden=512))
+    try:
+        shape = Qwen3Shape(hidden=512, layers=2, heads=4, kv_heads=2, head_dim=128, inter=1024,
+                           vocab=4096, max_pos=4096)
+        W = random_weights(shape, seed=21)
+        runner = ModelRunner(shape.hf_config(), rank=rank, world_size=world, max_num_seqs=8,
+                             max_seq_len=4096, device=dev)
+        runner.load_weights(W.items())
+        runner.allocate_kv_cache(8)
+        runner.kv_cache.zero_()
+        okv = OM.OracleKV(shape, 8, 256)
+        cs = _table_cpu(shape.max_pos, shape.head_dim, float(shape.theta))
+        g = torch.Generator().manual_seed(22)
+        seqs = [SeqState(torch.randint(0, 4096, (n,), generator=g).tolist(), 0, n, [2 * i, 2 * i + 1])
+                for i, n in enumerate((9, 300, 77))]
+        runner.capture_cudagraph([4])
+        for step in range(3):
+            meta = prepare_seqs(seqs, 256)
+            octx = {k: meta[k] for k in ("cu_seqlens_q", "cu_seqlens_k", "slot_mapping",
+                                         "block_tables", "is_prefill")}
+            ref = OM.compute_logits(shape, W, OM.forward(shape, W, meta["input_ids"], meta["positions"],
+                                                         octx, okv, tp=world, cos_sin=cs), octx)
+            ids, pos, ctx = runner.prepare(seqs)
+            logits = runner.run_model(ids, pos, ctx)
+            torch.cuda.synchronize()
+            if rank == 0:
+                err = L.rel_err(logits.cpu(), ref)
+                assert err <= 2e-2, (step, err)
+            for s, t in zip(seqs, ref.float().argmax(-1).tolist()):
+                s.num_cached_tokens = len(s.token_ids)
+                s.token_ids.append(int(t))
+                s.num_scheduled_tokens = 1
+        assert tp_comm.get().fused_calls > 0
+        assert b200.device_error(clear=True) == 0
+        runner.release_graphs()
+    finally:
+        tp_comm.clear()
+        dist.destroy_process_group()
+
+
+@pytest.fixture
+def two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+
+
+def test_fused_row_parallel_allreduce(two_gpus):
+    import torch.multiprocessing as mp
+    mp.spawn(_fused_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def test_qwen3_tp2_matches_oracle(two_gpus):
+    import torch.multiprocessing as mp
+    mp.spawn(_model_worker, args=(2, _free_port()), nprocs=2, join=True)
