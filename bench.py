@@ -559,6 +559,86 @@ def run_microbench(args):
                               "kernels": res, "peak_gbs": hbm}), flush=True)
 
 
+def run_allreduce_microbench(args, rank: int, world: int):
+    """Fused RowParallelLinear (GEMM + all-reduce over NVLink) of the Qwen3-8B
+    decode step at TP = world, T = 256 tokens: o_proj (K = 4096 / world) and
+    down_proj (K = 12288 / world), N = 4096.  Device time per call with CUDA
+    events, max over ranks, against GEMM + NCCL all_reduce.  Roofline target
+    = slowest of FLOPs / tensor peak, HBM bytes / HBM peak and NVLink bytes /
+    770 GB/s (measured peer-copy bandwidth per direction), with NVLink bytes
+    per rank = 2 (world - 1) / world x T x N x 2 (reduce-scatter + all-gather)."""
+    import datetime
+    import torch.distributed as dist
+    from src import b200
+    from src.layers.tp_allreduce import FusedRowParallel
+    torch.cuda.set_device(rank % torch.cuda.device_count())
+    dev = torch.device("cuda", torch.cuda.current_device())
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=4096)
+    hbm, tflops, kind = peaks()
+    nvlink = 770.0
+    T, N = 256, 4096
+    out = {}
+    stream = torch.cuda.current_stream()
+
+    def time_fn(fn):
+        """Device time per call: `steps` calls captured in one CUDA graph, the
+        graph replayed after warm-up (no host launch gaps), max over ranks."""
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                fn()
+        for _ in range(2):
+            graph.replay()
+        dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.inference_mode():
+        for name, Kfull in (("o_proj", 4096), ("down_proj", 12288)):
+            K = Kfull // world
+            g = torch.Generator(device=dev).manual_seed(rank + 1)
+            x = torch.randn(T, K, device=dev, generator=g).to(torch.bfloat16)
+            w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            fused_ms = time_fn(lambda: comm.linear_allreduce(x, w))
+
+            def unfused():
+                y = b200.linear(x, w)
+                dist.all_reduce(y)
+            base_ms = time_fn(unfused)
+            gemm_ms = time_fn(lambda: b200.linear(x, w))
+            yy = b200.linear(x, w)
+            nccl_ms = time_fn(lambda: dist.all_reduce(yy))
+            flops = 2.0 * T * N * K
+            hbm_bytes = N * K * 2 + T * K * 2 + T * N * 2
+            nv_bytes = 2.0 * (world - 1) / world * T * N * 2
+            target_ms = max(flops / (tflops * 1e12), hbm_bytes / (hbm * 1e9), nv_bytes / (nvlink * 1e9)) * 1e3
+            out[name] = {"K_per_rank": K, "fused_ms": fused_ms, "gemm_plus_nccl_ms": base_ms,
+                         "gemm_only_ms": gemm_ms, "nccl_allreduce_ms": nccl_ms,
+                         "roofline_ms": target_ms, "frac": target_ms / fused_ms,
+                         "nvlink_bytes_per_rank": nv_bytes, "hbm_bytes": hbm_bytes}
+    fused_ok = comm.fallback_calls == 0
+    comm.close()
+    if rank == 0:
+        print(json.dumps({"workload": "fused-rowparallel-allreduce (Qwen3-8B decode, T=256)",
+                          "tp": world, "kernels": out, "fused_path_taken": fused_ok,
+                          "nvlink_gbs_per_direction": nvlink, "hbm_peak_gbs": hbm,
+                          "tensor_peak_tflops": tflops, "peak_source": kind}), flush=True)
+    dist.barrier(device_ids=[dev.index])
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -570,7 +650,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-fused-ar", dest="fused_ar", action="store_false")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attn", "gemm"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "attn", "gemm", "allreduce"],
                     help="decode = the headline line; attn / gemm = kernel microbenchmarks")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "decode":
@@ -579,6 +659,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.workload == "allreduce":
+        run_allreduce_microbench(args, rank, world)
         return
     if args.workload != "decode":
         run_microbench(args)

@@ -88,13 +88,19 @@ int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long l
  * bf16(x_r * w_r^T (+ bias on rank 0)), the all-reduce of
  * src/layers/linear.py:169-173 (torch.distributed.all_reduce after F.linear)
  * fused into the GEMM epilogue over NVLink peer memory.  Every rank calls it
- * with the same shapes; stage / out / flags / done are arrays of `world`
- * device pointers giving each rank's address of its symmetric buffers
- * (rank r's own entry at index r):
- *   stage[r]: bf16 [world][stage_rows][ldo]   partials received by rank r
- *   out[r]:   bf16 [stage_rows][ldo]          reduced output on rank r
- *   flags[r], done[r]: uint32 [max_positions], zero before the first call
- *                       (every call leaves them zero)
+ * with the same shapes and the same `one_shot`; stage / out / flags / done
+ * are arrays of `world` device pointers giving each rank's address of its
+ * symmetric buffers (rank r's own entry at index r), zero before the first
+ * call:
+ *   one_shot == 0 (two-shot: partials to the owner of each output part,
+ *   which reduces and writes every rank's copy; 2 (world-1)/world of the
+ *   output bytes cross NVLink per rank):
+ *     stage[r]: bf16 [world][stage_rows][ldo]; out[r]: bf16 [stage_rows][ldo]
+ *     flags[r], done[r]: uint32 [max_positions] (left zero by every call)
+ *   one_shot != 0 (every rank pushes its partial to every rank and reduces
+ *   its own copy: one NVLink hop, world - 1 times the output bytes):
+ *     stage[r]: bf16 [2][world][stage_rows][ldo]; out[r] as above
+ *     flags[r]: uint32 [2][max_positions]; done[r]: uint32 [2] call counters
  * The reduced y is in out[rank] (rows [0, T), columns [0, N)) when the
  * launch completes on this rank's stream.  Returns B200_ERR_UNSUPPORTED
  * without launching when the CTAs of the launch could not all be resident
@@ -105,7 +111,7 @@ int b200_linear_allreduce(const void* x, long long ldx, const void* w, long long
                           const void* bias, int T, int N, int K, int rank, int world,
                           void* const* stage, void* const* out, void* const* flags,
                           void* const* done, long long stage_rows, long long ldo,
-                          long long max_positions, b200_stream_t stream);
+                          long long max_positions, int one_shot, b200_stream_t stream);
 
 /* CUDA IPC helpers for the symmetric buffers: export the allocation that
  * holds `ptr` (64-byte handle + offset of ptr inside it), map a peer's

@@ -298,7 +298,16 @@ int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ld
   if (int r = ensure_smem(ds, 1u, gemm_tn_tcgen05_kernel, p.smem)) return r;
   // every CTA must be resident at once (owners wait for peers' CTAs): take the
   // largest K split, down to none, whose grid fits the co-resident slots
+  // co-resident CTAs for a split (occupancy queries are slow: cached per
+  // device, split and shared-memory size)
+  static long long resident_cache[kMaxDevices][9][4] = {};
+  static int resident_smem[kMaxDevices][9][4] = {};
+  int dev_id = 0;
+  cudaGetDevice(&dev_id);
   auto resident_for = [&](int splits) -> long long {
+    for (int i = 0; i < 4; ++i)
+      if (resident_smem[dev_id][splits][i] == p.smem) return resident_cache[dev_id][splits][i];
+    const long long v = [&]() -> long long {
     if (splits == 1) {
       int per_sm = 0;
       if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_tn_tcgen05_kernel, kGemmThreads,
@@ -325,6 +334,14 @@ int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ld
       clusters = 0;
     }
     return (long long)clusters * splits;
+    }();
+    for (int i = 0; i < 4; ++i)
+      if (resident_smem[dev_id][splits][i] == 0) {
+        resident_smem[dev_id][splits][i] = p.smem;
+        resident_cache[dev_id][splits][i] = v;
+        break;
+      }
+    return v;
   };
   const long long tiles = (long long)p.n_tiles * p.token_tiles;
   int splits = p.splits;
@@ -671,7 +688,7 @@ int b200_linear_allreduce(const void* x, long long ldx, const void* w, long long
                           const void* bias, int T, int N, int K, int rank, int world,
                           void* const* stage, void* const* out, void* const* flags,
                           void* const* done, long long stage_rows, long long ldo,
-                          long long max_positions, b200_stream_t stream) {
+                          long long max_positions, int one_shot, b200_stream_t stream) {
   if (world < 1 || world > kMaxTpRanks || !stage || !out || !flags || !done)
     return fail(B200_ERR_INVALID, "linear_allreduce: world %d / peer arrays", world);
   AllReducePeers ar{};
@@ -679,6 +696,8 @@ int b200_linear_allreduce(const void* x, long long ldx, const void* w, long long
   ar.world = world;
   ar.stage_rows = stage_rows;
   ar.ldo = ldo;
+  ar.oneshot = one_shot ? 1 : 0;
+  ar.positions = max_positions;
   for (int r = 0; r < world; ++r) {
     ar.stage[r] = static_cast<__nv_bfloat16*>(stage[r]);
     ar.out[r] = static_cast<__nv_bfloat16*>(out[r]);

@@ -48,12 +48,12 @@ constexpr int kMaxTpRanks = 8;
 // Symmetric buffers of the fused GEMM + all-reduce (EPI_ALLREDUCE); index r
 // holds rank r's address of each buffer (this rank's own entry included).
 struct AllReducePeers {
-  __nv_bfloat16* stage[kMaxTpRanks];  // [world][stage_rows][ldo] partial products
+  __nv_bfloat16* stage[kMaxTpRanks];  // two-shot: [world][rows][ldo]; one-shot: [2][world][rows][ldo]
   __nv_bfloat16* out[kMaxTpRanks];    // [stage_rows][ldo] reduced output
-  unsigned* flags[kMaxTpRanks];       // per CTA position: partials received (owner side)
-  unsigned* done[kMaxTpRanks];        // per CTA position: reduced rows written (every rank)
-  int rank, world;
-  long long stage_rows, ldo;
+  unsigned* flags[kMaxTpRanks];       // two-shot: [positions]; one-shot: [2][positions]
+  unsigned* done[kMaxTpRanks];        // two-shot: [positions]; one-shot: call counter + exit counter
+  int rank, world, oneshot;
+  long long stage_rows, ldo, positions;
 };
 
 constexpr int kGemmBM = 128;
@@ -279,6 +279,82 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         for (int i = 0; i < 8 && feat + i < p.silu_inter; ++i) dst[i] = __float2bfloat16_rn(o[i]);
       }
     }
+  } else if (p.epi == EPI_ALLREDUCE && p.ar.oneshot) {
+    // ---- one-shot all-reduce: every rank pushes its bf16 partial of this CTA
+    // position into every rank's staging (peer stores), then sums the world's
+    // partials for its own copy.  Staging and flags alternate between two
+    // halves by call parity, read from a device-side call counter, so a rank
+    // that is already one call ahead never overwrites data still being read.
+    const AllReducePeers& ar = p.ar;
+    const unsigned pos = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    unsigned* calls = ar.done[ar.rank];
+    const unsigned parity = __ldcg(calls) & 1u;
+    const size_t half = (size_t)ar.world * ar.stage_rows * ar.ldo;
+    const int units = (te - tb) * 16;
+    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+      const int t = tb + (u >> 4), ch = u & 15;
+      const int n = n0 + ch * 8;
+      if (n >= p.N) continue;
+      float v[8];
+      sum8(t * kGemmBM + ch * 8, v);
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+      }
+      uint4 pk;
+      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
+      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
+      const size_t off = parity * half + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n;
+      for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.stage[r] + off) = pk;
+    }
+    __syncthreads();
+    __shared__ int s_ok1;
+    if (threadIdx.x == 0) {
+      // release at system scope orders the CTA's peer stores (made visible to
+      // this thread by the barrier above) before the flag
+      for (int r = 0; r < ar.world; ++r)
+        if (r != ar.rank) red_release_sys_add(ar.flags[r] + parity * ar.positions + pos, 1u);
+      s_ok1 = ar.world == 1 ||
+              wait_flag_and_reset(ar.flags[ar.rank] + parity * ar.positions + pos,
+                                  (unsigned)(ar.world - 1), p.err);
+    }
+    __syncthreads();
+    if (s_ok1) {
+      for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+        const int t = tb + (u >> 4), ch = u & 15;
+        const int n = n0 + ch * 8;
+        if (n >= p.N) continue;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
+          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
+              ar.stage[ar.rank] + parity * half + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
+          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16x2(qw[k]);
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
+        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(ar.out[ar.rank] + (size_t)(t0 + t) * ar.ldo + n) = pk;
+      }
+    }
+    // the last CTA to finish advances the call counter (every rank runs the
+    // same calls, so the counters stay equal)
+    if (threadIdx.x == 0) {
+      const unsigned nctas = gridDim.x * gridDim.y * gridDim.z;
+      __threadfence();
+      if (atomicAdd(calls + 1, 1u) == nctas - 1) {
+        atomicExch(calls + 1, 0u);
+        atomicAdd(calls, 1u);
+      }
+    }
   } else if (p.epi == EPI_ALLREDUCE) {
     // ---- fused all-reduce over NVLink peer memory (RowParallelLinear at tp > 1,
     // src/layers/linear.py:169-173).  Position = (token tile, feature tile,
@@ -306,10 +382,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       *reinterpret_cast<uint4*>(stage_dst + (size_t)(t0 + t) * ar.ldo + n) = pk;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      red_release_sys_add(ar.flags[owner] + pos, 1u);
-    }
+    if (threadIdx.x == 0) red_release_sys_add(ar.flags[owner] + pos, 1u);
     if (owner == ar.rank) {
       __shared__ int s_ok;
       if (threadIdx.x == 0) s_ok = wait_flag_and_reset(ar.flags[ar.rank] + pos, (unsigned)ar.world, p.err);
@@ -341,11 +414,9 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         }
       }
       __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence_system();
+      if (threadIdx.x == 0)
         for (int r = 0; r < ar.world; ++r)
           if (r != ar.rank) red_release_sys_add(ar.done[r] + pos, 1u);
-      }
     } else {
       // the owner writes this rank's copy of the reduced rows; wait for it so
       // that the kernel's completion means the output is complete here

@@ -40,7 +40,7 @@ _SIGNATURES = {
     "b200_linear_silu_and_mul": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _ll, _i, _i, _i,
                                   _c_void_p, _sz, _c_void_p], _i),
     "b200_linear_allreduce": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _i, _i, _i, _i, _i,
-                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _ll, _ll, _ll,
+                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _ll, _ll, _ll, _i,
                                _c_void_p], _i),
     "b200_ipc_export": ([_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_ulonglong)], _i),
     "b200_ipc_import": ([_c_void_p, ctypes.c_ulonglong, ctypes.POINTER(_c_void_p)], _i),
@@ -245,7 +245,8 @@ def ipc_close(ptr: int, offset: int) -> None:
 
 def linear_allreduce(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, rank: int,
                      world: int, stage: list[int], out: list[int], flags: list[int],
-                     done: list[int], stage_rows: int, ldo: int, max_positions: int) -> int:
+                     done: list[int], stage_rows: int, ldo: int, max_positions: int,
+                     one_shot: bool = False) -> int:
     """Fused GEMM + all-reduce; returns the C status (0, or ERR_UNSUPPORTED when
     the caller must fall back) and raises on any other failure."""
     lib = load_library()
@@ -258,7 +259,8 @@ def linear_allreduce(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None
     arr = ctypes.c_void_p * world
     rc = lib.b200_linear_allreduce(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(bias), x2.shape[0],
                                    w.shape[0], K, rank, world, arr(*stage), arr(*out), arr(*flags),
-                                   arr(*done), stage_rows, ldo, max_positions, _stream())
+                                   arr(*done), stage_rows, ldo, max_positions, int(one_shot),
+                                   _stream())
     if rc not in (0, ERR_UNSUPPORTED):
         _check(rc, "b200_linear_allreduce")
     return rc

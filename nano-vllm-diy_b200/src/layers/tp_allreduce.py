@@ -7,10 +7,17 @@ that owns that part of the output, the owner sums the world's partials in a
 fixed rank order and writes the result into every rank's output buffer
 (libb200ops: b200_linear_allreduce).
 
+Two exchange patterns (the same on every rank):
+  one-shot (world <= 4): every rank pushes its partial to every rank and
+    sums its own copy -- one NVLink hop;
+  two-shot (larger worlds): partials go to the owner of each output part,
+    which sums and writes every rank's copy -- 2 (w-1)/w of the bytes.
+
 Symmetric memory: every rank allocates one device buffer holding
-  stage  bf16 [world][max_tokens][ldo]   partials this rank owns
-  out    bf16 [2][max_tokens][ldo]       reduced outputs (ping-pong)
-  flags, done  uint32 [MAX_POSITIONS]    handshake counters (start at zero)
+  stage  bf16 [halves][world][max_tokens][ldo]  partials received
+  out    bf16 [2][max_tokens][ldo]              reduced outputs (ping-pong)
+  flags  uint32 [halves][MAX_POSITIONS], done uint32 [MAX_POSITIONS]
+with halves = 2 for one-shot (alternating by call parity), 1 for two-shot.
 and exchanges its CUDA IPC handle through the default process group (after
 init_process_group, outside graph capture), so every rank knows every
 rank's address of each part.
@@ -35,7 +42,7 @@ MAX_POSITIONS = 4096
 class FusedRowParallel:
 
     def __init__(self, device: torch.device, max_tokens: int = 512, max_hidden: int = 8192,
-                 group=None):
+                 group=None, one_shot: bool | None = None):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -44,10 +51,14 @@ class FusedRowParallel:
         self.device = device
         self.max_tokens = max_tokens
         self.ldo = (max_hidden + 7) // 8 * 8
+        # one NVLink hop for small worlds; for larger ones the owner-reduce
+        # (two-shot) moves 2 (w-1)/w instead of (w-1) times the output bytes
+        self.one_shot = self.world <= 4 if one_shot is None else one_shot
+        halves = 2 if self.one_shot else 1
         elt = 2
-        self.stage_bytes = self.world * max_tokens * self.ldo * elt
+        self.stage_bytes = halves * self.world * max_tokens * self.ldo * elt
         self.out_bytes = max_tokens * self.ldo * elt
-        flag_bytes = MAX_POSITIONS * 4
+        flag_bytes = halves * MAX_POSITIONS * 4
         self.off_stage = 0
         self.off_out = [self.stage_bytes, self.stage_bytes + self.out_bytes]
         self.off_flags = self.stage_bytes + 2 * self.out_bytes
@@ -90,7 +101,7 @@ class FusedRowParallel:
             rc = b200.linear_allreduce(
                 x, w, bias, self.rank, self.world, self._addrs(self.off_stage),
                 self._addrs(self.off_out[idx]), self._addrs(self.off_flags),
-                self._addrs(self.off_done), self.max_tokens, self.ldo, MAX_POSITIONS)
+                self._addrs(self.off_done), self.max_tokens, self.ldo, MAX_POSITIONS, self.one_shot)
             if rc == 0:
                 self._flip ^= 1
                 self.fused_calls += 1
