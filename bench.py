@@ -574,7 +574,8 @@ def run_allreduce_microbench(args, rank: int, world: int):
     torch.cuda.set_device(rank % torch.cuda.device_count())
     dev = torch.device("cuda", torch.cuda.current_device())
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=4096)
+    mode = {"auto": None, "oneshot": True, "twoshot": False}[args.ar_mode]
+    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=4096, one_shot=mode)
     hbm, tflops, kind = peaks()
     nvlink = 770.0
     T, N = 256, 4096
@@ -632,7 +633,8 @@ def run_allreduce_microbench(args, rank: int, world: int):
     comm.close()
     if rank == 0:
         print(json.dumps({"workload": "fused-rowparallel-allreduce (Qwen3-8B decode, T=256)",
-                          "tp": world, "kernels": out, "fused_path_taken": fused_ok,
+                          "tp": world, "mode": "one-shot" if comm.one_shot else "two-shot",
+                          "kernels": out, "fused_path_taken": fused_ok,
                           "nvlink_gbs_per_direction": nvlink, "hbm_peak_gbs": hbm,
                           "tensor_peak_tflops": tflops, "peak_source": kind}), flush=True)
     dist.barrier(device_ids=[dev.index])
@@ -650,6 +652,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-fused-ar", dest="fused_ar", action="store_false")
+    ap.add_argument("--ar-mode", default="auto", choices=["auto", "oneshot", "twoshot"],
+                    help="fused all-reduce exchange (allreduce workload)")
     ap.add_argument("--workload", default="decode", choices=["decode", "attn", "gemm", "allreduce"],
                     help="decode = the headline line; attn / gemm = kernel microbenchmarks")
     args = ap.parse_args()

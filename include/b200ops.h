@@ -92,9 +92,10 @@ int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long l
  * are arrays of `world` device pointers giving each rank's address of its
  * symmetric buffers (rank r's own entry at index r), zero before the first
  * call:
- *   one_shot == 0 (two-shot: partials to the owner of each output part,
- *   which reduces and writes every rank's copy; 2 (world-1)/world of the
- *   output bytes cross NVLink per rank):
+ *   one_shot == 0 (two-shot: the rows of every CTA position are split among
+ *   the ranks; each rank's CTA gathers and reduces its share and writes it
+ *   into every rank's output; 2 (world-1)/world of the output bytes cross
+ *   NVLink per rank):
  *     stage[r]: bf16 [world][stage_rows][ldo]; out[r]: bf16 [stage_rows][ldo]
  *     flags[r], done[r]: uint32 [max_positions] (left zero by every call)
  *   one_shot != 0 (every rank pushes its partial to every rank and reduces

@@ -28,11 +28,13 @@
 //
 // Epilogues:
 //   EPI_BF16     y = bf16(acc + bias)
-//   EPI_ALLREDUCE  RowParallelLinear at tp > 1: the bf16 partial of every
-//                CTA position goes by NVLink peer stores to the position's
-//                owner rank, which sums the world's partials in fp32 (fixed
-//                rank order) and stores the bf16 result into every rank's
-//                output buffer; flag handshakes are bounded waits
+//   EPI_ALLREDUCE  RowParallelLinear at tp > 1, the all-reduce fused over
+//                NVLink peer stores.  one-shot: every rank pushes its bf16
+//                partial to every rank and sums its own copy.  two-shot: the
+//                rows of each CTA position are split among the ranks' CTAs
+//                of that position; each sums its rows from the world's
+//                partials (fp32, fixed rank order) and stores them into
+//                every rank's output.  Flag handshakes are bounded waits.
 //   EPI_SILU     tiles hold 64 gate rows + the 64 matching up rows of the
 //                [gate ; up] weight; y = bf16(silu(bf16 g) * bf16 u)
 //                (src/layers/activation.py:6-10 fused into the gate_up GEMM)
@@ -87,6 +89,17 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 __device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_relaxed_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// One system-scope fence (cumulative over the CTA's writes ordered by the
+// preceding barrier), then a relaxed increment of every peer's flag: one
+// fence per signal instead of one per peer.
+__device__ __forceinline__ void signal_peers(unsigned* const* flags, size_t index, int rank, int world) {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  for (int r = 0; r < world; ++r)
+    if (r != rank) red_relaxed_sys_add(flags[r] + index, 1u);
 }
 // Bounded wait until *p == want; resets *p to 0 afterwards (the flag is
 // consumed).  Returns false and records ERR_PEER_TIMEOUT after 1 s.
@@ -311,10 +324,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     __syncthreads();
     __shared__ int s_ok1;
     if (threadIdx.x == 0) {
-      // release at system scope orders the CTA's peer stores (made visible to
-      // this thread by the barrier above) before the flag
-      for (int r = 0; r < ar.world; ++r)
-        if (r != ar.rank) red_release_sys_add(ar.flags[r] + parity * ar.positions + pos, 1u);
+      signal_peers(ar.flags, parity * ar.positions + pos, ar.rank, ar.world);
       s_ok1 = ar.world == 1 ||
               wait_flag_and_reset(ar.flags[ar.rank] + parity * ar.positions + pos,
                                   (unsigned)(ar.world - 1), p.err);
@@ -356,15 +366,19 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       }
     }
   } else if (p.epi == EPI_ALLREDUCE) {
-    // ---- fused all-reduce over NVLink peer memory (RowParallelLinear at tp > 1,
-    // src/layers/linear.py:169-173).  Position = (token tile, feature tile,
-    // cluster rank); its owner rank sums the world's partials.
+    // ---- two-shot all-reduce over NVLink peer memory, spread evenly over
+    // the CTAs that share this position (same tile on every rank): the
+    // position's token rows are cut into `world` sub-slices; rank r's CTA
+    // reduces sub-slice r.  Phase 1: push sub-slice s of this rank's bf16
+    // partial to rank s.  Phase 2: when the world's partials of sub-slice
+    // `rank` are in, sum them (fixed rank order) and store the result into
+    // every rank's output.  Phase 3: wait until the other sub-slices have
+    // arrived here, so the kernel's completion means the output is complete.
     const AllReducePeers& ar = p.ar;
     const unsigned pos = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    const int owner = (int)(pos % (unsigned)ar.world);
-    const int units = (te - tb) * 16;
-    __nv_bfloat16* stage_dst = ar.stage[owner] + (size_t)ar.rank * ar.stage_rows * ar.ldo;
-    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+    const int rows = te - tb;
+    const int sub = (rows + ar.world - 1) / ar.world;
+    for (int u = threadIdx.x; u < rows * 16; u += kGemmThreads) {
       const int t = tb + (u >> 4), ch = u & 15;
       const int n = n0 + ch * 8;
       if (n >= p.N) continue;
@@ -375,54 +389,52 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         for (int i = 0; i < 8; ++i)
           if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
       }
-      // this rank's partial, rounded to bf16 as F.linear's output is
       uint4 pk;
       pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
       pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
-      *reinterpret_cast<uint4*>(stage_dst + (size_t)(t0 + t) * ar.ldo + n) = pk;
+      const int dst = (t - tb) / sub;  // rank reducing this row
+      *reinterpret_cast<uint4*>(ar.stage[dst] + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n) = pk;
     }
     __syncthreads();
-    if (threadIdx.x == 0) red_release_sys_add(ar.flags[owner] + pos, 1u);
-    if (owner == ar.rank) {
-      __shared__ int s_ok;
-      if (threadIdx.x == 0) s_ok = wait_flag_and_reset(ar.flags[ar.rank] + pos, (unsigned)ar.world, p.err);
-      __syncthreads();
-      if (s_ok) {
-        for (int u = threadIdx.x; u < units; u += kGemmThreads) {
-          const int t = tb + (u >> 4), ch = u & 15;
-          const int n = n0 + ch * 8;
-          if (n >= p.N) continue;
-          float acc[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-          for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
-            const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
-                ar.stage[ar.rank] + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
-            const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = unpack_bf16x2(qw[k]);
-              acc[2 * k] += f.x;
-              acc[2 * k + 1] += f.y;
-            }
-          }
-          uint4 pk;
-          pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
-          pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
-          for (int r = 0; r < ar.world; ++r)
-            *reinterpret_cast<uint4*>(ar.out[r] + (size_t)(t0 + t) * ar.ldo + n) = pk;
-        }
-      }
-      __syncthreads();
-      if (threadIdx.x == 0)
-        for (int r = 0; r < ar.world; ++r)
-          if (r != ar.rank) red_release_sys_add(ar.done[r] + pos, 1u);
-    } else {
-      // the owner writes this rank's copy of the reduced rows; wait for it so
-      // that the kernel's completion means the output is complete here
-      if (threadIdx.x == 0) wait_flag_and_reset(ar.done[ar.rank] + pos, 1u, p.err);
-      __syncthreads();
+    __shared__ int s_ok2;
+    if (threadIdx.x == 0) {
+      signal_peers(ar.flags, pos, ar.rank, ar.world);
+      s_ok2 = wait_flag_and_reset(ar.flags[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
     }
+    __syncthreads();
+    const int mb = tb + ar.rank * sub, me = min(te, mb + sub);
+    if (s_ok2) {
+      for (int u = threadIdx.x; u < max(0, me - mb) * 16; u += kGemmThreads) {
+        const int t = mb + (u >> 4), ch = u & 15;
+        const int n = n0 + ch * 8;
+        if (n >= p.N) continue;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
+          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
+              ar.stage[ar.rank] + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
+          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16x2(qw[k]);
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
+        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
+        for (int r = 0; r < ar.world; ++r)
+          *reinterpret_cast<uint4*>(ar.out[r] + (size_t)(t0 + t) * ar.ldo + n) = pk;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      signal_peers(ar.done, pos, ar.rank, ar.world);
+      wait_flag_and_reset(ar.done[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
+    }
+    __syncthreads();
   } else {
     const int units = (te - tb) * 16;
     for (int u = threadIdx.x; u < units; u += kGemmThreads) {

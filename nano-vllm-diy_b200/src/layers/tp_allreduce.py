@@ -8,10 +8,11 @@ fixed rank order and writes the result into every rank's output buffer
 (libb200ops: b200_linear_allreduce).
 
 Two exchange patterns (the same on every rank):
-  one-shot (world <= 4): every rank pushes its partial to every rank and
+  one-shot (world == 2): every rank pushes its partial to every rank and
     sums its own copy -- one NVLink hop;
-  two-shot (larger worlds): partials go to the owner of each output part,
-    which sums and writes every rank's copy -- 2 (w-1)/w of the bytes.
+  two-shot (larger worlds): the rows of each output part are split among
+    the ranks; each sums its rows and writes them to every rank -- 2 (w-1)/w
+    of the bytes (measured faster from 4 ranks up).
 
 Symmetric memory: every rank allocates one device buffer holding
   stage  bf16 [halves][world][max_tokens][ldo]  partials received
@@ -53,7 +54,7 @@ class FusedRowParallel:
         self.ldo = (max_hidden + 7) // 8 * 8
         # one NVLink hop for small worlds; for larger ones the owner-reduce
         # (two-shot) moves 2 (w-1)/w instead of (w-1) times the output bytes
-        self.one_shot = self.world <= 4 if one_shot is None else one_shot
+        self.one_shot = self.world <= 2 if one_shot is None else one_shot
         halves = 2 if self.one_shot else 1
         elt = 2
         self.stage_bytes = halves * self.world * max_tokens * self.ldo * elt

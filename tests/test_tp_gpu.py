@@ -36,7 +36,7 @@ def _init(rank, world, port):
     return torch.device("cuda", rank)
 
 
-def _fused_worker(rank, world, port):
+def _fused_worker(rank, world, port, one_shot):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
     sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "nano-vllm-diy_b200")]
@@ -45,7 +45,7 @@ def _fused_worker(rank, world, port):
     from src import b200
     from src.layers.tp_allreduce import FusedRowParallel
     dev = _init(rank, world, port)
-    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=4096)
+    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=4096, one_shot=one_shot)
     try:
         N, K = 4096, 2048
         for T in (1, 7, 64, 256, 300, 512):
@@ -140,9 +140,10 @@ def two_gpus():
         pytest.skip("needs 2 GPUs")
 
 
-def test_fused_row_parallel_allreduce(two_gpus):
+@pytest.mark.parametrize("one_shot", [True, False], ids=["one-shot", "two-shot"])
+def test_fused_row_parallel_allreduce(two_gpus, one_shot):
     import torch.multiprocessing as mp
-    mp.spawn(_fused_worker, args=(2, _free_port()), nprocs=2, join=True)
+    mp.spawn(_fused_worker, args=(2, _free_port(), one_shot), nprocs=2, join=True)
 
 
 def test_qwen3_tp2_matches_oracle(two_gpus):
