@@ -2,10 +2,10 @@
 
 The reference computes y_r = F.linear(x_r, W_r) on every rank and sums with
 torch.distributed.all_reduce (src/layers/linear.py:169-173).  Here one kernel
-per rank does both: each CTA's bf16 partial goes by peer stores to the rank
-that owns that part of the output, the owner sums the world's partials in a
-fixed rank order and writes the result into every rank's output buffer
-(libb200ops: b200_linear_allreduce).
+per rank does both: each CTA's bf16 partial goes by NVLink peer stores to
+the rank(s) that reduce it, the world's partials are summed in a fixed rank
+order (identical results on every rank), and the result lands in every
+rank's output buffer (libb200ops: b200_linear_allreduce).
 
 Two exchange patterns (the same on every rank):
   one-shot (world == 2): every rank pushes its partial to every rank and
@@ -18,7 +18,7 @@ Symmetric memory: every rank allocates one device buffer holding
   stage  bf16 [halves][world][max_tokens][ldo]  partials received
   out    bf16 [2][max_tokens][ldo]              reduced outputs (ping-pong)
   flags  uint32 [halves][MAX_POSITIONS], done uint32 [MAX_POSITIONS]
-with halves = 2 for one-shot (alternating by call parity), 1 for two-shot.
+with halves = 2 for one-shot (alternating by call parity), 1 for two-shot,
 and exchanges its CUDA IPC handle through the default process group (after
 init_process_group, outside graph capture), so every rank knows every
 rank's address of each part.
