@@ -431,7 +431,7 @@ def run_b200(args, rank: int, world: int):
     step_bytes = w_bytes + kv_bytes * shape.layers + B * runner.local_kv_heads * 128 * 4 * shape.layers
     step_gbs = step_bytes / (ms / 1000.0) / 1e9
     traffic = None
-    tpath = os.path.join(REPO, "profiles", "decode_attention_traffic.json")
+    tpath = os.path.join(REPO, "profiles", "decode_attention_traffic.txt")
     if os.path.exists(tpath):
         try:
             with open(tpath) as f:
