@@ -267,12 +267,10 @@ def run_b200(args, rank: int, world: int):
         dist.init_process_group("nccl", device_id=dev,
                                 timeout=__import__("datetime").timedelta(seconds=120))
         if args.fused_ar:
-            try:
-                from src.layers import tp_allreduce
-            except ImportError:
-                args.fused_ar = False
-            else:
-                tp_comm.set_comm(tp_allreduce.FusedRowParallel.create(dev))
+            from src.layers import tp_allreduce
+            tp_comm.set_comm(tp_allreduce.FusedRowParallel.create(dev))
+        else:
+            tp_comm.set_enabled(False)
     shape = qwen3_8b_config()
     cfg = shape.hf_config()
     B = args.batch

@@ -4,8 +4,8 @@ Same classes, constructor arguments, parameter shapes and `weight_loader`
 protocol as src/layers/linear.py of nano-vllm-diy, so checkpoints load through
 the reference loader unchanged.  forward() runs libb200ops' GEMM;
 RowParallelLinear at tp > 1 runs the GEMM and the sum over ranks as one fused
-kernel when a tensor-parallel communicator is set up (src.layers.tp_comm),
-and otherwise the GEMM followed by torch.distributed.all_reduce.
+kernel through the process's tensor-parallel communicator (src.layers.tp_comm,
+created on first use), and otherwise the GEMM followed by torch.distributed.all_reduce.
 """
 from __future__ import annotations
 
@@ -164,7 +164,7 @@ class RowParallelLinear(LinearBase):
         if self.tp_world_size == 1:
             return b200.linear(x, self.weight, bias)
         from src.layers import tp_comm
-        comm = tp_comm.get()
+        comm = tp_comm.ensure(x.device, self.out_features)
         if comm is not None:
             return comm.linear_allreduce(x, self.weight, bias)
         y = b200.linear(x, self.weight, bias)
