@@ -19,7 +19,9 @@ import os
 import torch
 
 _PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-LIB_PATH = os.path.join(_PKG, "lib", "libb200ops.so")
+# B200_OPS_LIB points at the library when these modules are copied into
+# another `src` tree (the reference checkout); default: the package's lib/
+LIB_PATH = os.environ.get("B200_OPS_LIB") or os.path.join(_PKG, "lib", "libb200ops.so")
 
 _lib = None
 
