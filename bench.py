@@ -556,15 +556,29 @@ def run_microbench(args):
             res = {}
             for name, (N, K) in shapes.items():
                 x = torch.randn(T, K, device=dev).to(torch.bfloat16)
-                w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+                # enough weight copies that consecutive calls stream from HBM
+                # (> 300 MB between reuses of one copy, L2 is 126 MB)
+                copies = max(1, -(-300 * 2 ** 20 // (N * K * 2)))
+                ws = [(torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+                y = torch.empty(T, N // 2 if name == "gate_up" else N, device=dev, dtype=torch.bfloat16)
                 if name == "gate_up":
-                    fn = lambda: b200.linear_silu_and_mul(x, w)
+                    fn = lambda w: b200.linear_silu_and_mul(x, w, out=y)
                 else:
-                    fn = lambda: b200.linear(x, w)
-                ms = timeit(fn)
+                    fn = lambda w: b200.linear(x, w, out=y)
+                # device time per call from a CUDA graph of `per` calls (a
+                # host-launched loop would time the Python launch path)
+                fn(ws[0])
+                torch.cuda.synchronize()
+                per = 2 * copies if copies > 1 else 10
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for i in range(per):
+                        fn(ws[i % copies])
+                ms = timeit(graph.replay) / per
+                del graph, ws
                 byts = N * K * 2 + T * K * 2 + T * (N // 2 if name == "gate_up" else N) * 2
                 res[name] = {"ms": ms, "gbs": byts / ms / 1e6, "frac": byts / ms / 1e6 / hbm}
-                del x, w
+                del x
             print(json.dumps({"workload": "gemm-microbench (Qwen3-8B TP1 decode, T=256)",
                               "kernels": res, "peak_gbs": hbm}), flush=True)
 

@@ -57,9 +57,10 @@ int b200_device_error(unsigned* out, int clear);
  * Linear layers
  * ------------------------------------------------------------------------ */
 
-/* Workspace bytes b200_linear needs for this shape: always 0 (split-K
- * partials are summed on chip through cluster shared memory); kept so that
- * callers can size buffers without knowing the kernel's tiling. */
+/* Workspace bytes b200_linear / b200_linear_silu_and_mul use: the stream-K
+ * flags and fp32 partial tiles of the persistent SM-pair GEMM (4 KiB +
+ * 128 KiB per SM, the same for every shape).  The workspace must be
+ * zero-filled before its first use; every call leaves it reusable. */
 int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes);
 
 /* y[T, N] = x[T, K] * w[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate,
@@ -68,7 +69,10 @@ int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes);
  *   src/layers/linear.py:169-170 RowParallelLinear.forward (per-rank part)
  *   src/layers/llm_head.py:64    ParallelLMHead.forward
  * K, ldx and ldw must be multiples of 8; x and w 16-byte aligned.
- * `workspace` / `ws_bytes` are accepted and unused (may be NULL / 0). */
+ * With a workspace of b200_linear_workspace_bytes() bytes (zeroed once,
+ * 16-byte aligned) the GEMM runs on the persistent SM-pair kernel
+ * (tcgen05.mma.cta_group::2, stream-K); with NULL it runs on the single-SM
+ * kernel.  Concurrent calls must not share one workspace. */
 int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
                 void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
                 b200_stream_t stream);
@@ -79,7 +83,7 @@ int b200_linear(const void* x, long long ldx, const void* w, long long ldw, cons
  *   src/layers/linear.py:74-75 + src/layers/activation.py:6-10.
  * w is [2I, K] with rows [gate ; up] exactly as MergedColumnParallelLinear
  * stores them (src/layers/linear.py:89-102).  I must be a multiple of 64
- * (B200_ERR_UNSUPPORTED otherwise); workspace is unused. */
+ * (B200_ERR_UNSUPPORTED otherwise); workspace as for b200_linear. */
 int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long long ldw, void* y,
                              long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
                              b200_stream_t stream);

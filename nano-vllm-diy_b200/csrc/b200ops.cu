@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "elementwise.cuh"
 #include "gemm.cuh"
+#include "gemm_pair.cuh"
 #include "../../include/b200ops.h"
 
 using namespace b200;
@@ -128,6 +129,24 @@ PFN_cuMemGetAddressRange_v3020 address_range_fn() {
   return fn;
 }
 
+// 2-D bf16 tensor map with the given swizzle (zero fill outside on loads,
+// clipping on stores).
+int make_tmap_sw(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                 uint64_t row_stride, uint32_t box_inner, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle) {
+  auto enc = tensor_map_encoder();
+  if (enc == nullptr) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride * 2};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return B200_OK;
+}
+
 // 2-D bf16 tensor map: `rows` rows of `inner` elements, `row_stride` elements
 // apart, box = box_inner x box_rows, 128-byte swizzle, zero fill outside.
 int make_tmap(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
@@ -227,8 +246,122 @@ GemmPlan plan_gemm(DeviceState* ds, int T, int N, int K, bool silu_tiles) {
   return p;
 }
 
+// ---------------------------------------------------------------------------
+// SM-pair GEMM (gemm_pair_tcgen05_kernel): one CTA per SM, clusters (2, 1, S)
+// ---------------------------------------------------------------------------
+constexpr int kPairSmemBudget = 224 * 1024;
+
+// B200_GEMM_PAIR=0 selects the single-SM kernel for every shape and
+// B200_GEMM_PAIR=2 the SM-pair kernel for every shape (read at every call, so
+// a process can compare the two kernels).
+bool pair_enabled() {
+  const char* e = getenv("B200_GEMM_PAIR");
+  return !(e && *e == '0');
+}
+bool pair_forced() {
+  const char* e = getenv("B200_GEMM_PAIR");
+  return e && *e == '2';
+}
+
+// Co-resident CTAs of the pair kernel with clusters of (2, 1, splits) and the
+// given dynamic shared memory (occupancy queries are slow: cached).
+long long pair_resident(int splits, int smem) {
+  static long long cache[kMaxDevices][5][4] = {};
+  static int cache_smem[kMaxDevices][5][4] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices || splits < 1 || splits > 4) return 0;
+  for (int i = 0; i < 4; ++i)
+    if (cache_smem[dev][splits][i] == smem) return cache[dev][splits][i];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, splits);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_tcgen05_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    clusters = 0;
+  }
+  const long long v = (long long)clusters * 2 * splits;
+  for (int i = 0; i < 4; ++i)
+    if (cache_smem[dev][splits][i] == 0) {
+      cache_smem[dev][splits][i] = smem;
+      cache[dev][splits][i] = v;
+      break;
+    }
+  return v;
+}
+
+// Workspace of the persistent pair kernel: 4 KiB of partial-ready flags,
+// then one fp32 [256][128] partial tile per CTA (at most one CTA per SM).
+size_t pair_workspace_bytes(int num_sms) { return 4096 + (size_t)num_sms * 256 * kGemmBM * 4; }
+
+// Plan of the persistent SM-pair kernel: tokens in tiles of 256 (128 per
+// CTA), BN = NP = the pair's weight rows per tile (<= 256; the gate_up
+// projection always 256 = 128 gate + the 128 matching up rows), n_tiles =
+// 2 x feature tiles, TMEM = two accumulators of pow2(NP) columns.
+// `splits` holds the number of pairs launched: as many as can be resident,
+// with at least max(4, K blocks / 4) units of work each.
+GemmPlan plan_pair(DeviceState* ds, int T, int N, int K, bool silu_tiles, int* rc) {
+  GemmPlan p{};
+  p.BN = silu_tiles ? 256 : std::min(256, std::max(32, round_up(N, 32)));
+  p.token_tiles = (T + 2 * kGemmBM - 1) / (2 * kGemmBM);
+  p.n_tiles = 2 * (silu_tiles ? (N / 2 + 127) / 128 : (N + p.BN - 1) / p.BN);
+  p.num_kb = (K + kGemmBK - 1) / kGemmBK;
+  const int stage = kGemmBM * kGemmBK * 2 + (p.BN / 2) * kGemmBK * 2;
+  const int extra = 2 * kGemmBM * 64 + 512;  // output staging + barriers
+  p.stages = std::min(kGemmMaxStages, (kPairSmemBudget - 1024 - extra) / stage);
+  p.smem = 1024 + p.stages * stage + extra;
+  int cols = 32;
+  while (cols < p.BN) cols <<= 1;
+  p.tmem_cols = 2 * cols;
+  *rc = ensure_smem(ds, 8u, gemm_pair_tcgen05_kernel, p.smem);
+  if (*rc) return p;
+  const long long total = (long long)(p.n_tiles / 2) * p.token_tiles * p.num_kb;
+  long long pairs = pair_resident(1, p.smem) / 2;
+  pairs = std::min(pairs, (long long)ds->num_sms / 2);
+  // every pair takes at least a quarter of a tile's K blocks, so a tile is
+  // shared by at most 5 pairs (a finisher streams <= 4 partials)
+  const long long min_units = std::max(4, (p.num_kb + 3) / 4);
+  pairs = std::max(1LL, std::min(pairs, total / min_units));
+  const char* forced = getenv("B200_GEMM_PAIRS");
+  if (forced && *forced) pairs = std::max(1LL, std::min(pairs, (long long)atoi(forced)));
+  p.splits = (int)pairs;
+  if (gemm_debug())
+    fprintf(stderr, "[b200 gemm pair] T=%d N=%d K=%d NP=%d tiles=%dx%d kb=%d pairs=%d stages=%d smem=%d\n",
+            T, N, K, p.BN, p.n_tiles / 2, p.token_tiles, p.num_kb, p.splits, p.stages, p.smem);
+  return p;
+}
+
+int launch_pair(const GemmPlan& p, const CUtensorMap& tmW, const CUtensorMap& tmX,
+                const CUtensorMap& tmY, const GemmArgs& a, cudaStream_t st, const char* what) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * p.splits, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_tcgen05_kernel, tmW, tmX, tmY, a);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
+}
+
 int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const void* bias, void* y,
-             long long ldy, int T, int N, int K, bool silu, cudaStream_t st) {
+             long long ldy, int T, int N, int K, bool silu, void* workspace, size_t ws_bytes,
+             cudaStream_t st) {
   if (T <= 0) return B200_OK;
   if (N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "linear: bad shape N=%d K=%d", N, K);
   if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K)
@@ -239,6 +372,51 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
   if (!silu && ldy < N) return fail(B200_ERR_INVALID, "linear: ldy < N");
   DeviceState* ds;
   if (int r = device_state(&ds)) return r;
+  // the SM-pair kernel when every pair gets at least one whole tile (large
+  // projections such as gate_up and the LM head: measured faster there);
+  // smaller problems would be mostly stream-K fix-ups, where the single-SM
+  // kernel's on-chip split-K is faster
+  const long long pair_tiles = (long long)(silu ? (N / 2 + 127) / 128 : (N + 255) / 256) *
+                               ((T + 2 * kGemmBM - 1) / (2 * kGemmBM));
+  if (pair_enabled() && workspace != nullptr && aligned16(workspace) &&
+      ws_bytes >= pair_workspace_bytes(ds->num_sms) &&
+      (pair_tiles >= ds->num_sms / 2 || pair_forced())) {
+    int prc = 0;
+    const GemmPlan p = plan_pair(ds, T, N, K, silu, &prc);
+    if (prc) return prc;
+    CUtensorMap tmW, tmX;
+    if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK,
+                          (uint32_t)(p.BN / 2)))
+      return r;
+    if (int r = make_tmap(&tmX, x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx, kGemmBK,
+                          (uint32_t)kGemmBM))
+      return r;
+    GemmArgs a{};
+    a.T = T; a.N = N; a.K = K; a.BN = p.BN; a.stages = p.stages; a.num_kb = p.num_kb;
+    a.kb_per_split = p.kb_per_split; a.splits = p.splits; a.tmem_cols = p.tmem_cols;
+    a.epi = silu ? EPI_SILU : EPI_BF16;
+    a.vec_ok = aligned16(y) && (ldy % 8 == 0);
+    a.y = static_cast<__nv_bfloat16*>(y); a.ldy = ldy;
+    a.bias = static_cast<const __nv_bfloat16*>(bias);
+    a.silu_inter = N / 2;
+    a.tiles_m = p.n_tiles / 2;
+    a.tiles_t = p.token_tiles;
+    a.sk_flags = static_cast<unsigned*>(workspace);
+    a.sk_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + 4096);
+    a.err = ds->err;
+    // outputs by TMA tensor stores: box of 32 features x 128 tokens, 64-byte
+    // swizzle (the kernel's staging layout)
+    CUtensorMap tmY;
+    std::memset(&tmY, 0, sizeof(tmY));
+    a.use_tma_store = 0;
+    if (a.vec_ok) {
+      const uint64_t cols = silu ? (uint64_t)(N / 2) : (uint64_t)N;
+      if (make_tmap_sw(&tmY, y, cols, (uint64_t)T, (uint64_t)ldy, 32, (uint32_t)kGemmBM,
+                       CU_TENSOR_MAP_SWIZZLE_64B) == B200_OK)
+        a.use_tma_store = 1;
+    }
+    return launch_pair(p, tmW, tmX, tmY, a, st, "gemm_pair_tcgen05_kernel");
+  }
   const GemmPlan p = plan_gemm(ds, T, N, K, silu);
   CUtensorMap tmW, tmX;
   if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK,
@@ -417,23 +595,24 @@ int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes) {
   if (!bytes || T < 0 || N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "bad arguments");
   DeviceState* ds;
   if (int r = device_state(&ds)) return r;
-  (void)ds;
-  *bytes = 0;  // split-K partials are reduced on chip (cluster shared memory)
+  // the persistent SM-pair kernel's stream-K flags and partial tiles (the
+  // same bound for every shape, so one buffer serves every GEMM)
+  *bytes = pair_workspace_bytes(ds->num_sms);
   return B200_OK;
 }
 
 int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
                 void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
                 b200_stream_t stream) {
-  (void)workspace; (void)ws_bytes;
-  return run_gemm(x, ldx, w, ldw, bias, y, ldy, T, N, K, false, reinterpret_cast<cudaStream_t>(stream));
+  return run_gemm(x, ldx, w, ldw, bias, y, ldy, T, N, K, false, workspace, ws_bytes,
+                  reinterpret_cast<cudaStream_t>(stream));
 }
 
 int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long long ldw, void* y,
                              long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
                              b200_stream_t stream) {
-  (void)workspace; (void)ws_bytes;
-  return run_gemm(x, ldx, w, ldw, nullptr, y, ldy, T, 2 * I, K, true, reinterpret_cast<cudaStream_t>(stream));
+  return run_gemm(x, ldx, w, ldw, nullptr, y, ldy, T, 2 * I, K, true, workspace, ws_bytes,
+                  reinterpret_cast<cudaStream_t>(stream));
 }
 
 int b200_rms_norm(const void* x, long long x_stride, const void* residual, const void* weight,

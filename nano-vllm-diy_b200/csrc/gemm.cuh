@@ -77,6 +77,12 @@ struct GemmArgs {
   long long ldy;       // row stride of y (elements)
   const __nv_bfloat16* bias;  // [N] or nullptr (EPI_BF16 only)
   int silu_inter;      // EPI_SILU: I (rows of W are [gate(I) ; up(I)])
+  // stream-K schedule of the persistent SM-pair kernel
+  int tiles_m;         // 256-row weight tiles (pairs of 128-row CTA tiles)
+  int tiles_t;         // token tiles of BN
+  unsigned* sk_flags;  // [pairs * 2] partial-ready flags (zero between launches)
+  float* sk_part;      // [pairs * 2][BN][128] fp32 partial tiles
+  int use_tma_store;   // outputs written by TMA tensor stores (needs y 16-byte aligned, ldy % 8 == 0)
   unsigned* err;
   AllReducePeers ar;   // EPI_ALLREDUCE only
 };
@@ -120,6 +126,203 @@ __device__ __forceinline__ float silu_mul_ref(float g, float u) {
   // again (eager semantics of src/layers/activation.py:9-10).
   const float s = bf16_round(g / (1.0f + expf(-g)));
   return bf16_round(__fmul_rn(s, u));
+}
+
+// Epilogue shared by the GEMM kernels: this CTA's token rows [tb, te) of
+// the tile at (token t0, feature n0 / SiLU tile ntile).  `sum8(off, v)`
+// returns the 8 fp32 accumulators at float offset `off` of the [token][128]
+// tile summed over the CTA's split-K group; `pos` / `nctas` identify the CTA
+// position in the grid (same on every rank) for the all-reduce handshakes.
+template <typename SumFn>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, SumFn& sum8, int t0, int n0,
+                                              int ntile, int tb, int te, unsigned pos,
+                                              unsigned nctas) {
+  if (p.epi == EPI_SILU) {
+    // 8 output features (8 gate + the 8 matching up rows) per unit
+    const int units = (te - tb) * 8;
+    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+      const int t = tb + (u >> 3), ch = u & 7;
+      const int feat = ntile * 64 + ch * 8;
+      if (feat >= p.silu_inter) continue;
+      float g[8], up[8], o[8];
+      sum8(t * kGemmBM + ch * 8, g);
+      sum8(t * kGemmBM + 64 + ch * 8, up);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = silu_mul_ref(bf16_round(g[i]), bf16_round(up[i]));
+      __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + feat;
+      if (p.vec_ok && feat + 8 <= p.silu_inter) {
+        uint4 pk;
+        pk.x = pack_bf16x2(o[0], o[1]); pk.y = pack_bf16x2(o[2], o[3]);
+        pk.z = pack_bf16x2(o[4], o[5]); pk.w = pack_bf16x2(o[6], o[7]);
+        *reinterpret_cast<uint4*>(dst) = pk;
+      } else {
+        for (int i = 0; i < 8 && feat + i < p.silu_inter; ++i) dst[i] = __float2bfloat16_rn(o[i]);
+      }
+    }
+  } else if (p.epi == EPI_ALLREDUCE && p.ar.oneshot) {
+    // ---- one-shot all-reduce: every rank pushes its bf16 partial of this CTA
+    // position into every rank's staging (peer stores), then sums the world's
+    // partials for its own copy.  Staging and flags alternate between two
+    // halves by call parity, read from a device-side call counter, so a rank
+    // that is already one call ahead never overwrites data still being read.
+    const AllReducePeers& ar = p.ar;
+    unsigned* calls = ar.done[ar.rank];
+    const unsigned parity = __ldcg(calls) & 1u;
+    const size_t half = (size_t)ar.world * ar.stage_rows * ar.ldo;
+    const int units = (te - tb) * 16;
+    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+      const int t = tb + (u >> 4), ch = u & 15;
+      const int n = n0 + ch * 8;
+      if (n >= p.N) continue;
+      float v[8];
+      sum8(t * kGemmBM + ch * 8, v);
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+      }
+      uint4 pk;
+      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
+      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
+      const size_t off = parity * half + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n;
+      for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.stage[r] + off) = pk;
+    }
+    __syncthreads();
+    __shared__ int s_ok1;
+    if (threadIdx.x == 0) {
+      signal_peers(ar.flags, parity * ar.positions + pos, ar.rank, ar.world);
+      s_ok1 = ar.world == 1 ||
+              wait_flag_and_reset(ar.flags[ar.rank] + parity * ar.positions + pos,
+                                  (unsigned)(ar.world - 1), p.err);
+    }
+    __syncthreads();
+    if (s_ok1) {
+      for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+        const int t = tb + (u >> 4), ch = u & 15;
+        const int n = n0 + ch * 8;
+        if (n >= p.N) continue;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
+          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
+              ar.stage[ar.rank] + parity * half + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
+          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16x2(qw[k]);
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
+        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(ar.out[ar.rank] + (size_t)(t0 + t) * ar.ldo + n) = pk;
+      }
+    }
+    // the last CTA to finish advances the call counter (every rank runs the
+    // same calls, so the counters stay equal)
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(calls + 1, 1u) == nctas - 1) {
+        atomicExch(calls + 1, 0u);
+        atomicAdd(calls, 1u);
+      }
+    }
+  } else if (p.epi == EPI_ALLREDUCE) {
+    // ---- two-shot all-reduce over NVLink peer memory, spread evenly over
+    // the CTAs that share this position (same tile on every rank): the
+    // position's token rows are cut into `world` sub-slices; rank r's CTA
+    // reduces sub-slice r.  Phase 1: push sub-slice s of this rank's bf16
+    // partial to rank s.  Phase 2: when the world's partials of sub-slice
+    // `rank` are in, sum them (fixed rank order) and store the result into
+    // every rank's output.  Phase 3: wait until the other sub-slices have
+    // arrived here, so the kernel's completion means the output is complete.
+    const AllReducePeers& ar = p.ar;
+    const int rows = te - tb;
+    const int sub = (rows + ar.world - 1) / ar.world;
+    for (int u = threadIdx.x; u < rows * 16; u += kGemmThreads) {
+      const int t = tb + (u >> 4), ch = u & 15;
+      const int n = n0 + ch * 8;
+      if (n >= p.N) continue;
+      float v[8];
+      sum8(t * kGemmBM + ch * 8, v);
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+      }
+      uint4 pk;
+      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
+      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
+      const int dst = (t - tb) / sub;  // rank reducing this row
+      *reinterpret_cast<uint4*>(ar.stage[dst] + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n) = pk;
+    }
+    __syncthreads();
+    __shared__ int s_ok2;
+    if (threadIdx.x == 0) {
+      signal_peers(ar.flags, pos, ar.rank, ar.world);
+      s_ok2 = wait_flag_and_reset(ar.flags[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
+    }
+    __syncthreads();
+    const int mb = tb + ar.rank * sub, me = min(te, mb + sub);
+    if (s_ok2) {
+      for (int u = threadIdx.x; u < max(0, me - mb) * 16; u += kGemmThreads) {
+        const int t = mb + (u >> 4), ch = u & 15;
+        const int n = n0 + ch * 8;
+        if (n >= p.N) continue;
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
+          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
+              ar.stage[ar.rank] + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
+          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16x2(qw[k]);
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
+        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
+        for (int r = 0; r < ar.world; ++r)
+          *reinterpret_cast<uint4*>(ar.out[r] + (size_t)(t0 + t) * ar.ldo + n) = pk;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      signal_peers(ar.done, pos, ar.rank, ar.world);
+      wait_flag_and_reset(ar.done[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
+    }
+    __syncthreads();
+  } else {
+    const int units = (te - tb) * 16;
+    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
+      const int t = tb + (u >> 4), ch = u & 15;
+      const int n = n0 + ch * 8;
+      if (n >= p.N) continue;
+      float v[8];
+      sum8(t * kGemmBM + ch * 8, v);
+      if (p.bias != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+      }
+      __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + n;
+      if (p.vec_ok && n + 8 <= p.N) {
+        uint4 pk;
+        pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
+        pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(dst) = pk;
+      } else {
+        for (int i = 0; i < 8 && n + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 2)
@@ -270,195 +473,8 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
     }
   };
-  if (p.epi == EPI_SILU) {
-    // 8 output features (8 gate + the 8 matching up rows) per unit
-    const int units = (te - tb) * 8;
-    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
-      const int t = tb + (u >> 3), ch = u & 7;
-      const int feat = ntile * 64 + ch * 8;
-      if (feat >= p.silu_inter) continue;
-      float g[8], up[8], o[8];
-      sum8(t * kGemmBM + ch * 8, g);
-      sum8(t * kGemmBM + 64 + ch * 8, up);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = silu_mul_ref(bf16_round(g[i]), bf16_round(up[i]));
-      __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + feat;
-      if (p.vec_ok && feat + 8 <= p.silu_inter) {
-        uint4 pk;
-        pk.x = pack_bf16x2(o[0], o[1]); pk.y = pack_bf16x2(o[2], o[3]);
-        pk.z = pack_bf16x2(o[4], o[5]); pk.w = pack_bf16x2(o[6], o[7]);
-        *reinterpret_cast<uint4*>(dst) = pk;
-      } else {
-        for (int i = 0; i < 8 && feat + i < p.silu_inter; ++i) dst[i] = __float2bfloat16_rn(o[i]);
-      }
-    }
-  } else if (p.epi == EPI_ALLREDUCE && p.ar.oneshot) {
-    // ---- one-shot all-reduce: every rank pushes its bf16 partial of this CTA
-    // position into every rank's staging (peer stores), then sums the world's
-    // partials for its own copy.  Staging and flags alternate between two
-    // halves by call parity, read from a device-side call counter, so a rank
-    // that is already one call ahead never overwrites data still being read.
-    const AllReducePeers& ar = p.ar;
-    const unsigned pos = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    unsigned* calls = ar.done[ar.rank];
-    const unsigned parity = __ldcg(calls) & 1u;
-    const size_t half = (size_t)ar.world * ar.stage_rows * ar.ldo;
-    const int units = (te - tb) * 16;
-    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
-      const int t = tb + (u >> 4), ch = u & 15;
-      const int n = n0 + ch * 8;
-      if (n >= p.N) continue;
-      float v[8];
-      sum8(t * kGemmBM + ch * 8, v);
-      if (p.bias != nullptr) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
-      }
-      uint4 pk;
-      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
-      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
-      const size_t off = parity * half + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n;
-      for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.stage[r] + off) = pk;
-    }
-    __syncthreads();
-    __shared__ int s_ok1;
-    if (threadIdx.x == 0) {
-      signal_peers(ar.flags, parity * ar.positions + pos, ar.rank, ar.world);
-      s_ok1 = ar.world == 1 ||
-              wait_flag_and_reset(ar.flags[ar.rank] + parity * ar.positions + pos,
-                                  (unsigned)(ar.world - 1), p.err);
-    }
-    __syncthreads();
-    if (s_ok1) {
-      for (int u = threadIdx.x; u < units; u += kGemmThreads) {
-        const int t = tb + (u >> 4), ch = u & 15;
-        const int n = n0 + ch * 8;
-        if (n >= p.N) continue;
-        float acc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
-          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
-              ar.stage[ar.rank] + parity * half + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = unpack_bf16x2(qw[k]);
-            acc[2 * k] += f.x;
-            acc[2 * k + 1] += f.y;
-          }
-        }
-        uint4 pk;
-        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
-        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4*>(ar.out[ar.rank] + (size_t)(t0 + t) * ar.ldo + n) = pk;
-      }
-    }
-    // the last CTA to finish advances the call counter (every rank runs the
-    // same calls, so the counters stay equal)
-    if (threadIdx.x == 0) {
-      const unsigned nctas = gridDim.x * gridDim.y * gridDim.z;
-      __threadfence();
-      if (atomicAdd(calls + 1, 1u) == nctas - 1) {
-        atomicExch(calls + 1, 0u);
-        atomicAdd(calls, 1u);
-      }
-    }
-  } else if (p.epi == EPI_ALLREDUCE) {
-    // ---- two-shot all-reduce over NVLink peer memory, spread evenly over
-    // the CTAs that share this position (same tile on every rank): the
-    // position's token rows are cut into `world` sub-slices; rank r's CTA
-    // reduces sub-slice r.  Phase 1: push sub-slice s of this rank's bf16
-    // partial to rank s.  Phase 2: when the world's partials of sub-slice
-    // `rank` are in, sum them (fixed rank order) and store the result into
-    // every rank's output.  Phase 3: wait until the other sub-slices have
-    // arrived here, so the kernel's completion means the output is complete.
-    const AllReducePeers& ar = p.ar;
-    const unsigned pos = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    const int rows = te - tb;
-    const int sub = (rows + ar.world - 1) / ar.world;
-    for (int u = threadIdx.x; u < rows * 16; u += kGemmThreads) {
-      const int t = tb + (u >> 4), ch = u & 15;
-      const int n = n0 + ch * 8;
-      if (n >= p.N) continue;
-      float v[8];
-      sum8(t * kGemmBM + ch * 8, v);
-      if (p.bias != nullptr) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
-      }
-      uint4 pk;
-      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
-      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
-      const int dst = (t - tb) / sub;  // rank reducing this row
-      *reinterpret_cast<uint4*>(ar.stage[dst] + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n) = pk;
-    }
-    __syncthreads();
-    __shared__ int s_ok2;
-    if (threadIdx.x == 0) {
-      signal_peers(ar.flags, pos, ar.rank, ar.world);
-      s_ok2 = wait_flag_and_reset(ar.flags[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
-    }
-    __syncthreads();
-    const int mb = tb + ar.rank * sub, me = min(te, mb + sub);
-    if (s_ok2) {
-      for (int u = threadIdx.x; u < max(0, me - mb) * 16; u += kGemmThreads) {
-        const int t = mb + (u >> 4), ch = u & 15;
-        const int n = n0 + ch * 8;
-        if (n >= p.N) continue;
-        float acc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
-          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
-              ar.stage[ar.rank] + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = unpack_bf16x2(qw[k]);
-            acc[2 * k] += f.x;
-            acc[2 * k + 1] += f.y;
-          }
-        }
-        uint4 pk;
-        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
-        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
-        for (int r = 0; r < ar.world; ++r)
-          *reinterpret_cast<uint4*>(ar.out[r] + (size_t)(t0 + t) * ar.ldo + n) = pk;
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      signal_peers(ar.done, pos, ar.rank, ar.world);
-      wait_flag_and_reset(ar.done[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
-    }
-    __syncthreads();
-  } else {
-    const int units = (te - tb) * 16;
-    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
-      const int t = tb + (u >> 4), ch = u & 15;
-      const int n = n0 + ch * 8;
-      if (n >= p.N) continue;
-      float v[8];
-      sum8(t * kGemmBM + ch * 8, v);
-      if (p.bias != nullptr) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
-      }
-      __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + n;
-      if (p.vec_ok && n + 8 <= p.N) {
-        uint4 pk;
-        pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
-        pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
-        *reinterpret_cast<uint4*>(dst) = pk;
-      } else {
-        for (int i = 0; i < 8 && n + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i]);
-      }
-    }
-  }
+  const unsigned pos = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  gemm_epilogue(p, sum8, t0, n0, ntile, tb, te, pos, gridDim.x * gridDim.y * gridDim.z);
   // peers may still be reading this CTA's tile
   if (splits > 1) cluster_sync();
 }

@@ -1,0 +1,507 @@
+// Y[T, N] = X[T, K] * W[N, K]^T on SM pairs: tcgen05.mma.cta_group::2.
+//
+// Two CTAs on the two SMs of a cluster issue one M = 256 MMA together: each
+// stages its own 128 token rows (A) and half of the pair's NP weight rows
+// (B); the MMA reads A from both CTAs and B from both halves, and each CTA's
+// TMEM receives its own 128 tokens x NP columns of the accumulator.  Per
+// 64-wide K block an SM ingests 32 KB for 128 x 256 x 64 MACs, half the
+// token bytes per weight byte of the single-SM kernel.
+//
+// Pair protocol (per 64-wide K block, stage s):
+//   both producers  wait own empty[s]; the leader arms its full[s] with the
+//                   bytes of both CTAs; both issue their TMA loads with
+//                   .cta_group::2, completing on the LEADER's full[s]
+//   leader MMA      waits full[s], issues 4 x (M=256, N=NP, K=16), then
+//                   commits to empty[s] of both CTAs (two commits addressed
+//                   through mapa), and after a tile to acc_full of both CTAs
+//   both epilogues  wait own acc_full, read their TMEM lanes, release the
+//                   accumulator to the leader's acc_empty
+// Every wait is bounded (kWaitLimitNs) and records an error bit.
+#pragma once
+#include "gemm.cuh"
+
+namespace b200 {
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// D[tmem] (+)= A * B^T over the CTA pair (issued by the leader only).
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the mbarrier at a shared::cluster address (this CTA's or the
+// peer's) once the pair MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          bar_cluster_addr)
+      : "memory");
+}
+// 2-D tiled load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair (given by its shared::cluster address).  Same
+// 16-byte rule on c0 as tma_load_2d (callers pass multiples of 64 elements).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t smem_dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster_addr, int32_t c0,
+                                                 int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// mbarrier arrive on a barrier given by its shared::cluster address (this
+// CTA's or the pair peer's), release at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   bar_cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void epi_bar_sync() {  // the 4 epilogue warps
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Contiguous global -> shared copy by the bulk-copy engine, completing
+// `bytes` on the mbarrier (addresses 16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_dst),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 2-D tiled store shared -> global by the TMA engine (clipped at the tensor
+// bounds), tracked by bulk async-groups.  c0 * element size must be a
+// multiple of 16 bytes and neither coordinate negative.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t smem_src, int32_t c0,
+                                             int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Stream-K range of pair `pr` of `pairs` over `total` K-block units.
+__device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs) {
+  return total * pr / pairs;
+}
+
+// ---------------------------------------------------------------------------
+// Persistent SM-pair GEMM with a stream-K schedule.
+//
+// Operand roles: the TOKENS are the M = 256 operand (128 per CTA of the pair,
+// TMEM lane = token) and the weight rows the N operand (the pair's NP
+// features, NP/2 staged by each CTA), so each epilogue thread owns one token
+// row and writes contiguous output features straight from its registers;
+// for the gate_up projection a tile's columns are [128 gate | the 128
+// matching up rows], so SiLU-and-mul needs no exchange between threads.
+//
+// grid = 2 x pairs CTAs (all co-resident), cluster (2, 1, 1).  The work is
+// the flat sequence of (tile, K block) units, tile = (feature tile m, token
+// tile t) with t fastest (tiles sharing weights run back to back); pair p
+// takes units [total p / P, total (p+1) / P).  A range cuts tiles into
+// segments:
+//   whole        all K blocks of a tile       -> epilogue writes the output
+//   contributor  first segment of a range that starts inside a tile (its
+//                tail K blocks)               -> fp32 partial to sk_part[p],
+//                                                flag sk_flags[p] = 1
+//   finisher     last segment of a range that ends inside a tile (its head
+//                K blocks)                    -> waits for the flags of the
+//                pairs p+1.. whose ranges start inside the tile, adds their
+//                partials, writes the output, resets those flags to 0
+// Contributions are the first thing a pair computes and finishes are the
+// last, so a finisher never waits on work queued behind a wait.
+// TMEM holds two accumulators (2 x NP columns): the MMA issuer fills one
+// while the epilogue warps drain the other.
+// ---------------------------------------------------------------------------
+
+// Partial tiles are [NP/32 chunks] of 16 KiB, each [8][128 tokens][4
+// features] fp32: a thread's 32 columns of a chunk are 8 float4 at stride
+// 2 KiB, so a warp's accesses are 512 contiguous bytes.  A finisher streams
+// them through up to kFixSlots 16 KiB slots of the (by then idle) stage ring.
+constexpr int kFixSlots = 12;
+constexpr int kChunkFloats = 32 * kGemmBM;
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_tcgen05_kernel(const __grid_constant__ CUtensorMap tmW,
+                             const __grid_constant__ CUtensorMap tmX,
+                             const __grid_constant__ CUtensorMap tmY, const GemmArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int S = p.stages;
+  const bool silu = p.epi == EPI_SILU;
+  constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;  // 16 KiB: 128 tokens
+  const int NP = p.BN;                                  // the pair's tile columns
+  const uint32_t b_bytes = (uint32_t)(NP / 2) * kGemmBK * 2;
+  uint8_t* a_smem = smem;
+  uint8_t* b_smem = smem + (size_t)S * kABytes;
+  // output staging for the TMA stores: 2 x [128 tokens][32 features] bf16,
+  // 64-byte rows with the 64-byte swizzle (16-byte chunk c of row r at
+  // chunk c ^ ((r >> 1) & 3)), 1 KiB aligned
+  uint8_t* stage_out = b_smem + (size_t)S * b_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + 2 * kGemmBM * 64);
+  uint64_t* empty = full + kGemmMaxStages;
+  uint64_t* acc_full = empty + kGemmMaxStages;   // [2] per CTA
+  uint64_t* acc_empty = acc_full + 2;            // [2] used in the leader
+  uint64_t* fix_bar = acc_empty + 2;             // [kFixSlots] stream-K partial loads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fix_bar + kFixSlots);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const uint32_t v = crank & 1u;  // 0: leader (issues the MMAs), 1: peer
+  const uint32_t leader = crank & ~1u;
+  const int pr = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+  const long long total = (long long)p.tiles_m * p.tiles_t * p.num_kb;
+  const long long u_begin = sk_begin(total, pr, pairs);
+  const long long u_end = sk_begin(total, pr + 1, pairs);
+  const uint32_t acc_stride = (uint32_t)p.tmem_cols / 2;  // columns per accumulator
+  // output features of a tile: NP (plain) or the 128 gate rows (SiLU)
+  const int tile_feats = silu ? 128 : NP;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(&acc_full[0], 1);
+    mbar_init(&acc_full[1], 1);
+    mbar_init(&acc_empty[0], 2);  // one release from each CTA's epilogue
+    mbar_init(&acc_empty[1], 2);
+    for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+    if (p.use_tma_store) tma_prefetch_desc(&tmY);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, (uint32_t)p.tmem_cols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised before either signals the other
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- producer (both CTAs): this CTA's 128 tokens and NP/2 weight rows
+    if (lane == 0) {
+      const uint32_t full_leader = map_to_rank(smem_u32(full), leader);
+      int it = 0;
+      bool ok = true;
+      for (long long u = u_begin; u < u_end && ok;) {
+        const long long tile = u / p.num_kb;
+        const int kbb = (int)(u - tile * p.num_kb);
+        const int kbe = (int)min((long long)p.num_kb, kbb + (u_end - u));
+        const int mt = (int)(tile / p.tiles_t);
+        const int tt = (int)(tile - (long long)mt * p.tiles_t);
+        const int tok = tt * 2 * kGemmBM + (int)v * kGemmBM;
+        // weight rows: plain = features mt*NP + v*NP/2; SiLU = gate rows
+        // (leader) or the matching up rows (peer) of features mt*128
+        const int wrow = silu ? (int)v * p.silu_inter + mt * 128 : mt * NP + (int)v * (NP / 2);
+        for (int kb = kbb; kb < kbe; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (uint32_t)(it / S) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, p.err)) {
+            ok = false;
+            break;
+          }
+          if (v == 0) mbar_arrive_expect_tx(&full[s], 2u * (kABytes + b_bytes));
+          const int kc = kb * kGemmBK;
+          const uint32_t bar = full_leader + (uint32_t)s * 8u;
+          tma_load_2d_pair(smem_u32(a_smem + (size_t)s * kABytes), &tmX, bar, kc, tok);
+          tma_load_2d_pair(smem_u32(b_smem + (size_t)s * b_bytes), &tmW, bar, kc, wrow);
+        }
+        u += kbe - kbb;
+      }
+      if (!ok && v == 0) {
+        // drain the copies still in flight before the CTA can exit
+        for (int j = max(0, it - S); j < it; ++j)
+          mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, p.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer (leader only): M = 256 tokens, N = NP columns
+    if (lane == 0 && v == 0) {
+      const uint32_t idesc = umma_idesc_bf16(2 * kGemmBM, NP);
+      const uint32_t empty_own = map_to_rank(smem_u32(empty), leader);
+      const uint32_t empty_peer = map_to_rank(smem_u32(empty), leader + 1u);
+      const uint32_t accf_own = map_to_rank(smem_u32(acc_full), leader);
+      const uint32_t accf_peer = map_to_rank(smem_u32(acc_full), leader + 1u);
+      int it = 0, seg = 0;
+      bool ok = true;
+      for (long long u = u_begin; u < u_end && ok; ++seg) {
+        const long long tile = u / p.num_kb;
+        const int kbb = (int)(u - tile * p.num_kb);
+        const int kbe = (int)min((long long)p.num_kb, kbb + (u_end - u));
+        const int b = seg & 1;
+        // the epilogues of both CTAs have drained this accumulator
+        if (!mbar_wait(&acc_empty[b], (((uint32_t)seg >> 1) & 1u) ^ 1u, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)b * acc_stride;
+        for (int kb = kbb; kb < kbe; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (uint32_t)(it / S) & 1u;
+          if (!mbar_wait(&full[s], ph, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(a_smem + (size_t)s * kABytes);
+          const uint32_t b_base = smem_u32(b_smem + (size_t)s * b_bytes);
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            tc_mma_f16_pair(d, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32),
+                            idesc, (kb != kbb || kk != 0) ? 1u : 0u);
+          }
+          tc_commit_pair(empty_own + (uint32_t)s * 8u);
+          tc_commit_pair(empty_peer + (uint32_t)s * 8u);
+        }
+        tc_commit_pair(accf_own + (uint32_t)b * 8u);
+        tc_commit_pair(accf_peer + (uint32_t)b * 8u);
+        u += kbe - kbb;
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5: TMEM lane quarters 2,3,0,1; thread = token
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // token inside this CTA's 128
+    const bool lead_thread = (warp == 2 && lane == 0);
+    const uint32_t acc_empty_leader = map_to_rank(smem_u32(acc_empty), leader);
+    const int nchunks = NP / 32;
+    // TMEM chunks in consumption order (SiLU: gate chunk m, then up chunk m)
+    auto chunk_at = [&](int i) { return silu ? ((i & 1) ? nchunks / 2 + (i >> 1) : (i >> 1)) : i; };
+    bool ok = true;
+    int seg = 0;
+    for (long long u = u_begin; u < u_end; ++seg) {
+      const long long tile = u / p.num_kb;
+      const int kbb = (int)(u - tile * p.num_kb);
+      const int kbe = (int)min((long long)p.num_kb, kbb + (u_end - u));
+      const int mt = (int)(tile / p.tiles_t);
+      const int tt = (int)(tile - (long long)mt * p.tiles_t);
+      const int tok = tt * 2 * kGemmBM + (int)v * kGemmBM + row;  // this thread's token
+      const int f_base = mt * tile_feats;
+      const bool contributor = kbb > 0;
+      const bool finisher = kbb == 0 && kbe < p.num_kb;
+      const int b = seg & 1;
+      if (ok) ok = mbar_wait(&acc_full[b], ((uint32_t)seg >> 1) & 1u, p.err);
+      tc_fence_after();
+      // contributors of this tile: pairs pr+1, ... whose ranges start inside it
+      const long long tile_end = (tile + 1) * p.num_kb;
+      int last_contrib = pr;
+      if (finisher) {
+        while (last_contrib + 1 < pairs && sk_begin(total, last_contrib + 1, pairs) < tile_end)
+          ++last_contrib;
+        __shared__ int s_flags_ok;
+        if (lead_thread) {
+          bool all = true;
+          for (int c = pr + 1; c <= last_contrib && all; ++c) {
+            unsigned* f = p.sk_flags + (size_t)c * 2 + v;
+            const unsigned long long t_start = globaltimer_ns();
+            while (ld_acquire_gpu(f) == 0u) {
+              if (globaltimer_ns() - t_start > kWaitLimitNs) {
+                raise_error(p.err, ERR_PEER_TIMEOUT);
+                all = false;
+                break;
+              }
+            }
+          }
+          s_flags_ok = all;
+        }
+        epi_bar_sync();
+        if (!s_flags_ok) last_contrib = pr;  // give up on the partials, keep going
+      }
+      const uint32_t d = tmem_base + (uint32_t)b * acc_stride + ((uint32_t)(q * 32) << 16);
+      float* my_part = p.sk_part + ((size_t)pr * 2 + v) * (size_t)NP * kGemmBM;
+      const int ncontrib = last_contrib - pr;
+      // finisher: contributor partials stream into the idle stage ring
+      const int ring_slots = min(kFixSlots, (int)(((size_t)S * (kABytes + b_bytes)) / (kChunkFloats * 4)));
+      const int copies = ncontrib * nchunks;
+      auto issue_copy = [&](int k) {  // copy k: TMEM chunk chunk_at(k / ncontrib) of contributor pr+1 + k % ncontrib
+        const int slot = k % ring_slots;
+        const int cq = pr + 1 + k % ncontrib;
+        const float* src = p.sk_part + ((size_t)cq * 2 + v) * (size_t)NP * kGemmBM +
+                           (size_t)chunk_at(k / ncontrib) * kChunkFloats;
+        mbar_arrive_expect_tx(&fix_bar[slot], kChunkFloats * 4);
+        bulk_load(smem_u32(smem) + (uint32_t)slot * kChunkFloats * 4, src, kChunkFloats * 4,
+                  &fix_bar[slot]);
+      };
+      if (copies > 0 && lead_thread) {
+        fence_proxy_async_smem();
+        for (int k = 0; k < min(copies, ring_slots); ++k) issue_copy(k);
+      }
+      float keep[32];  // SiLU: the gate chunk, held until its up chunk arrives
+      int outs = 0;    // output chunks staged in this segment (staging buffer = outs & 1)
+      for (int i = 0; i < nchunks; ++i) {
+        const int ch = chunk_at(i);
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(d + (uint32_t)(ch * 32), r);
+        tmem_ld_wait();
+        if (i == nchunks - 1) {
+          // the accumulator is drained: hand it back to the MMA issuer
+          tc_fence_before();
+          epi_bar_sync();
+          if (lead_thread) {
+            if (v == 0) mbar_arrive(&acc_empty[b]);
+            else mbar_arrive_cluster(acc_empty_leader + (uint32_t)b * 8u);
+          }
+        }
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = ok ? __uint_as_float(r[j]) : 0.f;
+        if (contributor) {
+          float4* dst = reinterpret_cast<float4*>(my_part + (size_t)ch * kChunkFloats) + row;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            __stcg(dst + j * kGemmBM,
+                   make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]));
+          continue;
+        }
+        if (ncontrib > 0) {
+          for (int c = 0; c < ncontrib; ++c) {
+            const int k = i * ncontrib + c;
+            const int slot = k % ring_slots;
+            if (!mbar_wait(&fix_bar[slot], (uint32_t)(k / ring_slots) & 1u, p.err)) continue;
+            const float4* src = reinterpret_cast<const float4*>(smem + (size_t)slot * kChunkFloats * 4) + row;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 f = src[j * kGemmBM];
+              acc[4 * j] += f.x; acc[4 * j + 1] += f.y; acc[4 * j + 2] += f.z; acc[4 * j + 3] += f.w;
+            }
+          }
+          // this chunk's slots are read: refill them with the copies ring_slots ahead
+          epi_bar_sync();
+          if (lead_thread) {
+            fence_proxy_async_smem();
+            for (int c = 0; c < ncontrib; ++c) {
+              const int k = i * ncontrib + c + ring_slots;
+              if (k < copies) issue_copy(k);
+            }
+          }
+        }
+        int f0, fmax;
+        if (silu) {
+          if ((i & 1) == 0) {  // gate chunk: keep it for the up chunk
+#pragma unroll
+            for (int j = 0; j < 32; ++j) keep[j] = acc[j];
+            continue;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = silu_mul_ref(bf16_round(keep[j]), bf16_round(acc[j]));
+          f0 = f_base + (ch - nchunks / 2) * 32;
+          fmax = p.silu_inter;
+        } else {
+          f0 = f_base + ch * 32;
+          fmax = p.N;
+          if (p.bias != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (f0 + j < fmax) acc[j] += __bfloat162float(p.bias[f0 + j]);
+          }
+        }
+        if (p.use_tma_store) {
+          // stage the chunk ([128 tokens][32 features] bf16) and let the TMA
+          // engine write it (rows past T / columns past the output width are
+          // clipped by the tensor map; boxes wholly outside are not issued)
+          const int row0 = tt * 2 * kGemmBM + (int)v * kGemmBM;
+          if (f0 >= fmax || row0 >= p.T) continue;
+          uint8_t* stg = stage_out + (outs & 1) * (kGemmBM * 64);
+          if (lead_thread) bulk_wait_group_read<1>();  // the store two chunks back has read it
+          epi_bar_sync();
+          const uint32_t sw = (uint32_t)((row >> 1) & 3);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(stg + row * 64 + ((j ^ sw) * 16)) =
+                make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
+                           pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]), pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
+          fence_proxy_async_smem();
+          epi_bar_sync();
+          if (lead_thread) {
+            tma_store_2d(&tmY, smem_u32(stg), f0, row0);
+            bulk_commit_group();
+          }
+          ++outs;
+          continue;
+        }
+        // this thread's token row: 32 consecutive features, 4 x 16 bytes
+        if (tok < p.T && f0 < fmax) {
+          __nv_bfloat16* dst = p.y + (size_t)tok * p.ldy + f0;
+          if (p.vec_ok && f0 + 32 <= fmax) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<uint4*>(dst)[j] =
+                  make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
+                             pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]), pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (f0 + j < fmax) dst[j] = __float2bfloat16_rn(acc[j]);
+          }
+        }
+      }
+      if (contributor) {
+        // publish the partial: every epilogue thread's stores, then the flag
+        __threadfence();
+        epi_bar_sync();
+        if (lead_thread) st_release_gpu(p.sk_flags + (size_t)pr * 2 + v, 1u);
+      } else if (ncontrib > 0) {
+        // the partials are consumed: reset their flags for the next launch
+        if (lead_thread)
+          for (int cq = pr + 1; cq <= last_contrib; ++cq) p.sk_flags[(size_t)cq * 2 + v] = 0u;
+      }
+      u += kbe - kbb;
+    }
+    if (lead_thread && p.use_tma_store) bulk_wait_group_all();  // outputs written before exit
+  }
+  // every TMEM read and remote arrive of both CTAs is done before the pair
+  // frees its TMEM and either CTA exits
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, (uint32_t)p.tmem_cols);
+  }
+}
+
+}  // namespace b200

@@ -171,6 +171,22 @@ def device_error(clear: bool = True) -> int:
 # ---------------------------------------------------------------------------
 # GEMMs
 # ---------------------------------------------------------------------------
+_gemm_ws_bytes: dict[int, int] = {}
+
+
+def _gemm_workspace(device: torch.device) -> torch.Tensor:
+    """The GEMM's stream-K workspace of this device (zeroed on allocation,
+    sized before any graph capture by the first eager call)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    n = _gemm_ws_bytes.get(idx)
+    if n is None:
+        size = ctypes.c_size_t(0)
+        _check(load_library().b200_linear_workspace_bytes(1, 1, 1, ctypes.byref(size)),
+               "b200_linear_workspace_bytes")
+        n = _gemm_ws_bytes[idx] = int(size.value)
+    return workspace("gemm", n, device)
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
            out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x @ w.T (+ bias); x [..., K], w [N, K] -> [..., N] (F.linear)."""
@@ -190,8 +206,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     y2 = out.view(-1, N)
     if w.stride(-1) != 1:
         raise ValueError("linear: weight rows must be contiguous")
+    ws = _gemm_workspace(x.device)
     _check(lib.b200_linear(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(bias), _p(y2), y2.stride(0),
-                           T, N, K, None, 0, _stream()), "b200_linear")
+                           T, N, K, _p(ws), ws.numel(), _stream()), "b200_linear")
     return out
 
 
@@ -217,8 +234,9 @@ def linear_silu_and_mul(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | No
     if out is None:
         out = torch.empty(*x.shape[:-1], I, dtype=x.dtype, device=x.device)
     y2 = out.view(-1, I)
+    ws = _gemm_workspace(x.device)
     _check(lib.b200_linear_silu_and_mul(_p(x2), x2.stride(0), _p(w), w.stride(0), _p(y2),
-                                        y2.stride(0), T, I, K, None, 0, _stream()),
+                                        y2.stride(0), T, I, K, _p(ws), ws.numel(), _stream()),
            "b200_linear_silu_and_mul")
     return out
 

@@ -50,6 +50,29 @@ def test_linear(T, N, K):
     assert err <= 1e-2, err
 
 
+@pytest.mark.parametrize("kernel,pairs", [("pair", ""), ("pair", "1"), ("pair", "3"), ("pair", "17"),
+                                          ("single", "")])
+@pytest.mark.parametrize("T,N,K", [(256, 4096, 4096), (77, 1280, 2048), (513, 768, 1024),
+                                   (256, 24576, 1024)])
+def test_linear_kernels_and_splits(T, N, K, kernel, pairs, monkeypatch):
+    """Both GEMM kernels (persistent SM-pair tcgen05.mma.cta_group::2 with a
+    stream-K schedule, and single-SM) give the same product within
+    tolerance, whatever number of pairs shares the work (whole tiles,
+    contributor / finisher segments)."""
+    from src import b200
+    monkeypatch.setenv("B200_GEMM_PAIR", "2" if kernel == "pair" else "0")
+    monkeypatch.setenv("B200_GEMM_PAIRS", pairs)
+    x = randn(T, K, seed=11)
+    w = randn(N, K, std=0.02, seed=12)
+    ref = x.float() @ w.float().t()
+    y = b200.linear(x.to(DEV), w.to(DEV))
+    g = b200.linear_silu_and_mul(x.to(DEV), w.to(DEV))
+    torch.cuda.synchronize()
+    assert L.rel_err(y.cpu(), ref) <= 1e-2
+    assert L.rel_err(g.cpu(), L.silu_and_mul(ref.to(torch.bfloat16))) <= 2e-2
+    assert b200.device_error(clear=True) == 0
+
+
 def test_linear_bias_and_strided_out():
     from src import b200
     T, N, K = 48, 640, 1024
