@@ -249,7 +249,7 @@ GemmPlan plan_gemm(DeviceState* ds, int T, int N, int K, bool silu_tiles) {
 // ---------------------------------------------------------------------------
 // SM-pair GEMM (gemm_pair_tcgen05_kernel): one CTA per SM, clusters (2, 1, S)
 // ---------------------------------------------------------------------------
-constexpr int kPairSmemBudget = 224 * 1024;
+constexpr int kPairSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in limit)
 
 // B200_GEMM_PAIR=0 selects the single-SM kernel for every shape and
 // B200_GEMM_PAIR=2 the SM-pair kernel for every shape (read at every call, so
@@ -316,7 +316,7 @@ GemmPlan plan_pair(DeviceState* ds, int T, int N, int K, bool silu_tiles, int* r
   p.n_tiles = 2 * (silu_tiles ? (N / 2 + 127) / 128 : (N + p.BN - 1) / p.BN);
   p.num_kb = (K + kGemmBK - 1) / kGemmBK;
   const int stage = kGemmBM * kGemmBK * 2 + (p.BN / 2) * kGemmBK * 2;
-  const int extra = 2 * kGemmBM * 64 + 512;  // output staging + barriers
+  const int extra = 4 * kGemmBM * 64 + 512;  // output staging + barriers
   p.stages = std::min(kGemmMaxStages, (kPairSmemBudget - 1024 - extra) / stage);
   p.smem = 1024 + p.stages * stage + extra;
   int cols = 32;

@@ -121,10 +121,14 @@ __device__ __forceinline__ bool wait_flag_and_reset(unsigned* p, unsigned want, 
   return true;
 }
 
-__device__ __forceinline__ float silu_mul_ref(float g, float u) {
-  // F.silu on a bf16 tensor rounds its result to bf16, the product rounds
-  // again (eager semantics of src/layers/activation.py:9-10).
-  const float s = bf16_round(g / (1.0f + expf(-g)));
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  // Eager semantics of src/layers/activation.py:9-10 on bf16 tensors: silu
+  // is rounded to bf16, then the product is rounded again.  The sigmoid uses
+  // the hardware exp2 / reciprocal paths (__expf, __fdividef): their last-bit
+  // fp32 differences from expf and IEEE division disappear in the bf16
+  // rounding except for rare one-ulp cases, and they are several times
+  // cheaper, which matters in a GEMM epilogue.
+  const float s = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
   return bf16_round(__fmul_rn(s, u));
 }
 
@@ -148,7 +152,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, SumFn& sum8, in
       sum8(t * kGemmBM + ch * 8, g);
       sum8(t * kGemmBM + 64 + ch * 8, up);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = silu_mul_ref(bf16_round(g[i]), bf16_round(up[i]));
+      for (int i = 0; i < 8; ++i) o[i] = silu_mul(bf16_round(g[i]), bf16_round(up[i]));
       __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + feat;
       if (p.vec_ok && feat + 8 <= p.silu_inter) {
         uint4 pk;

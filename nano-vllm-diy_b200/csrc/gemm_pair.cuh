@@ -118,6 +118,20 @@ __device__ __forceinline__ void bulk_wait_group_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// tcgen05.wait::ld that the compiler sees as producing `r`: uses of the
+// registers of an asynchronous TMEM load cannot move above the wait.
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+        "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+        "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
+
 // Stream-K range of pair `pr` of `pairs` over `total` K-block units.
 __device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs) {
   return total * pr / pairs;
@@ -173,11 +187,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t b_bytes = (uint32_t)(NP / 2) * kGemmBK * 2;
   uint8_t* a_smem = smem;
   uint8_t* b_smem = smem + (size_t)S * kABytes;
-  // output staging for the TMA stores: 2 x [128 tokens][32 features] bf16,
+  // output staging for the TMA stores: 4 x [128 tokens][32 features] bf16,
   // 64-byte rows with the 64-byte swizzle (16-byte chunk c of row r at
   // chunk c ^ ((r >> 1) & 3)), 1 KiB aligned
   uint8_t* stage_out = b_smem + (size_t)S * b_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + 2 * kGemmBM * 64);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + 4 * kGemmBM * 64);
   uint64_t* empty = full + kGemmMaxStages;
   uint64_t* acc_full = empty + kGemmMaxStages;   // [2] per CTA
   uint64_t* acc_empty = acc_full + 2;            // [2] used in the leader
@@ -372,33 +386,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int k = 0; k < min(copies, ring_slots); ++k) issue_copy(k);
       }
       float keep[32];  // SiLU: the gate chunk, held until its up chunk arrives
-      int outs = 0;    // output chunks staged in this segment (staging buffer = outs & 1)
+      int outs = 0;    // output chunks staged in this segment (staging buffer = outs & 3)
+      // the barrier after which every TMEM load of this accumulator is done
+      const int rel_i = nchunks >= 2 ? nchunks - 2 : 0;
+      uint32_t rc[32], rn[32];
+      tmem_ld_32x32b_x32(d + (uint32_t)(chunk_at(0) * 32), rc);
+      tmem_ld_wait_regs(rc);
       for (int i = 0; i < nchunks; ++i) {
         const int ch = chunk_at(i);
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(d + (uint32_t)(ch * 32), r);
-        tmem_ld_wait();
-        if (i == nchunks - 1) {
-          // the accumulator is drained: hand it back to the MMA issuer
-          tc_fence_before();
-          epi_bar_sync();
-          if (lead_thread) {
-            if (v == 0) mbar_arrive(&acc_empty[b]);
-            else mbar_arrive_cluster(acc_empty_leader + (uint32_t)b * 8u);
-          }
-        }
+        // the next chunk's TMEM load overlaps this chunk's work
+        if (i + 1 < nchunks) tmem_ld_32x32b_x32(d + (uint32_t)(chunk_at(i + 1) * 32), rn);
         float acc[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = ok ? __uint_as_float(r[j]) : 0.f;
+        for (int j = 0; j < 32; ++j) acc[j] = ok ? __uint_as_float(rc[j]) : 0.f;
+        bool staged = false;
+        int f0 = 0, row0 = 0;
+        uint8_t* stg = nullptr;
         if (contributor) {
           float4* dst = reinterpret_cast<float4*>(my_part + (size_t)ch * kChunkFloats) + row;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             __stcg(dst + j * kGemmBM,
                    make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]));
-          continue;
-        }
-        if (ncontrib > 0) {
+        } else {
           for (int c = 0; c < ncontrib; ++c) {
             const int k = i * ncontrib + c;
             const int slot = k % ring_slots;
@@ -410,75 +420,89 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               acc[4 * j] += f.x; acc[4 * j + 1] += f.y; acc[4 * j + 2] += f.z; acc[4 * j + 3] += f.w;
             }
           }
-          // this chunk's slots are read: refill them with the copies ring_slots ahead
-          epi_bar_sync();
-          if (lead_thread) {
-            fence_proxy_async_smem();
-            for (int c = 0; c < ncontrib; ++c) {
-              const int k = i * ncontrib + c + ring_slots;
-              if (k < copies) issue_copy(k);
+          bool out = true;
+          int fmax;
+          if (silu) {
+            if ((i & 1) == 0) {  // gate chunk: keep it for the up chunk
+#pragma unroll
+              for (int j = 0; j < 32; ++j) keep[j] = acc[j];
+              out = false;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) acc[j] = silu_mul(bf16_round(keep[j]), bf16_round(acc[j]));
+            }
+            f0 = f_base + (ch - nchunks / 2) * 32;
+            fmax = p.silu_inter;
+          } else {
+            f0 = f_base + ch * 32;
+            fmax = p.N;
+            if (p.bias != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (f0 + j < fmax) acc[j] += __bfloat162float(p.bias[f0 + j]);
+            }
+          }
+          if (out && p.use_tma_store) {
+            // stage the chunk ([128 tokens][32 features] bf16, 64-byte
+            // swizzle) for the TMA engine; rows past T / columns past the
+            // output width are clipped by the tensor map, boxes wholly
+            // outside are not issued
+            row0 = tt * 2 * kGemmBM + (int)v * kGemmBM;
+            if (f0 < fmax && row0 < p.T) {
+              stg = stage_out + (outs & 3) * (kGemmBM * 64);
+              const uint32_t sw = (uint32_t)((row >> 1) & 3);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4*>(stg + row * 64 + ((j ^ sw) * 16)) =
+                    make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
+                               pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]), pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
+              fence_proxy_async_smem();
+              staged = true;
+            }
+          } else if (out && tok < p.T && f0 < fmax) {
+            // this thread's token row: 32 consecutive features
+            __nv_bfloat16* dst = p.y + (size_t)tok * p.ldy + f0;
+            if (p.vec_ok && f0 + 32 <= fmax) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(dst)[j] =
+                    make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
+                               pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]), pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (f0 + j < fmax) dst[j] = __float2bfloat16_rn(acc[j]);
             }
           }
         }
-        int f0, fmax;
-        if (silu) {
-          if ((i & 1) == 0) {  // gate chunk: keep it for the up chunk
-#pragma unroll
-            for (int j = 0; j < 32; ++j) keep[j] = acc[j];
-            continue;
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = silu_mul_ref(bf16_round(keep[j]), bf16_round(acc[j]));
-          f0 = f_base + (ch - nchunks / 2) * 32;
-          fmax = p.silu_inter;
-        } else {
-          f0 = f_base + ch * 32;
-          fmax = p.N;
-          if (p.bias != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (f0 + j < fmax) acc[j] += __bfloat162float(p.bias[f0 + j]);
-          }
-        }
-        if (p.use_tma_store) {
-          // stage the chunk ([128 tokens][32 features] bf16) and let the TMA
-          // engine write it (rows past T / columns past the output width are
-          // clipped by the tensor map; boxes wholly outside are not issued)
-          const int row0 = tt * 2 * kGemmBM + (int)v * kGemmBM;
-          if (f0 >= fmax || row0 >= p.T) continue;
-          uint8_t* stg = stage_out + (outs & 1) * (kGemmBM * 64);
-          if (lead_thread) bulk_wait_group_read<1>();  // the store two chunks back has read it
-          epi_bar_sync();
-          const uint32_t sw = (uint32_t)((row >> 1) & 3);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(stg + row * 64 + ((j ^ sw) * 16)) =
-                make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
-                           pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]), pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
-          fence_proxy_async_smem();
+        if (i + 1 < nchunks) tmem_ld_wait_regs(rn);
+        // one barrier per chunk (contributors: only the TMEM release): the
+        // staging writes and partial-slot reads of every thread are done
+        if (!contributor || i == rel_i) {
+          if (i == rel_i) tc_fence_before();
           epi_bar_sync();
           if (lead_thread) {
-            tma_store_2d(&tmY, smem_u32(stg), f0, row0);
-            bulk_commit_group();
-          }
-          ++outs;
-          continue;
-        }
-        // this thread's token row: 32 consecutive features, 4 x 16 bytes
-        if (tok < p.T && f0 < fmax) {
-          __nv_bfloat16* dst = p.y + (size_t)tok * p.ldy + f0;
-          if (p.vec_ok && f0 + 32 <= fmax) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              reinterpret_cast<uint4*>(dst)[j] =
-                  make_uint4(pack_bf16x2(acc[8 * j], acc[8 * j + 1]), pack_bf16x2(acc[8 * j + 2], acc[8 * j + 3]),
-                             pack_bf16x2(acc[8 * j + 4], acc[8 * j + 5]), pack_bf16x2(acc[8 * j + 6], acc[8 * j + 7]));
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (f0 + j < fmax) dst[j] = __float2bfloat16_rn(acc[j]);
+            if (i == rel_i) {  // every TMEM load of this accumulator is done
+              if (v == 0) mbar_arrive(&acc_empty[b]);
+              else mbar_arrive_cluster(acc_empty_leader + (uint32_t)b * 8u);
+            }
+            if (staged) {
+              tma_store_2d(&tmY, smem_u32(stg), f0, row0);
+              bulk_commit_group();
+              bulk_wait_group_read<2>();  // the buffer written two chunks from now is free
+            }
+            if (ncontrib > 0) {  // refill this chunk's partial slots
+              fence_proxy_async_smem();
+              for (int c = 0; c < ncontrib; ++c) {
+                const int k = i * ncontrib + c + ring_slots;
+                if (k < copies) issue_copy(k);
+              }
+            }
           }
         }
+        if (staged) ++outs;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) rc[j] = rn[j];
       }
       if (contributor) {
         // publish the partial: every epilogue thread's stores, then the flag
