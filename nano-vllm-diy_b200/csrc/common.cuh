@@ -292,13 +292,24 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, u
 }
 
 // D = A(16x16, row) * B(16x8, col) + D ; bf16 inputs, f32 accumulators.
+// Register-only (not volatile): the compiler may interleave independent
+// accumulation chains.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],
                                                uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Transpose of an 8x8 b16 matrix held as an m8n8 fragment (thread t: row
+// t / 4, columns 2 (t % 4), +1): afterwards thread t holds the transposed
+// matrix's row t / 4 in the same packing.  Warp-collective: volatile, so the
+// compiler keeps it where every lane executes it.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
 
 __device__ __forceinline__ float fast_exp2(float x) { return exp2f(x); }

@@ -224,12 +224,15 @@ __global__ void __launch_bounds__(128, 1)
   issue_next();
   issue_next();
 
-  const int g = lane >> 2;           // MMA row = query head inside the group
-  const bool live_row = g < a.G;
-  const int mi = lane >> 3, rin = lane & 7;
-  uint32_t qa[8][4];
-  float o[16][4];
-  float m_run = -INFINITY, l_run = 0.f;
+  // Tokens are the MMA rows: S^T = K Q^T (m16n8k16: 16 tokens x 8 head
+  // columns, k over the head dim) and O^T = V^T P^T (16 dims x 8 head
+  // columns, k over tokens).  The G query heads of the kv head are columns
+  // 0..G-1; columns >= G carry unrelated rows and are never stored (every
+  // column is independent of the others).
+  const int g = lane >> 2, tq = lane & 3;  // fragment row group / column pair
+  uint32_t qb[8][2];                        // B fragments of Q^T, 8 k-steps of 16 dims
+  float ot[8][4];                            // O^T: 8 tiles of 16 dims
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // head columns 2tq, 2tq+1
   int consumed = 0;
 
   for (int t = 0; t < valid_issued; ++t) {
@@ -259,108 +262,127 @@ __global__ void __launch_bounds__(128, 1)
     }
 
     if (d.first) {
-      // A fragments of Q: rows 0-7 = heads (rows >= G unused), rows 8-15 zero
+      // B fragments of Q^T = ldmatrix of the Q rows (heads) per 8-dim chunk
 #pragma unroll
-      for (int kp = 0; kp < 4; ++kp) {
-        ldmatrix_x4(sQ + tswz(1024, rin, 4 * kp + mi), qa[2 * kp][0], qa[2 * kp][2],
-                    qa[2 * kp + 1][0], qa[2 * kp + 1][2]);
-        qa[2 * kp][1] = qa[2 * kp][3] = qa[2 * kp + 1][1] = qa[2 * kp + 1][3] = 0u;
-      }
+      for (int p4 = 0; p4 < 4; ++p4)
+        ldmatrix_x4(sQ + tswz(1024, lane & 7, 4 * p4 + (lane >> 3)), qb[2 * p4][0], qb[2 * p4][1],
+                    qb[2 * p4 + 1][0], qb[2 * p4 + 1][1]);
 #pragma unroll
-      for (int dt = 0; dt < 16; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
-      m_run = -INFINITY;
-      l_run = 0.f;
+      for (int md = 0; md < 8; ++md) ot[md][0] = ot[md][1] = ot[md][2] = ot[md][3] = 0.f;
+      m_run[0] = m_run[1] = -INFINITY;
+      l_run[0] = l_run[1] = 0.f;
     }
 
-    // S = Q K^T over the tile's 32 tokens (4 n-tiles of 8)
-    float sc[4][4];
+    // S^T over the tile's 32 tokens: 2 token tiles of 16
+    float sc[2][4];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    for (int mt = 0; mt < 2; ++mt) sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
 #pragma unroll
-    for (int kp = 0; kp < 4; ++kp) {
+    for (int kk = 0; kk < 8; ++kk) {
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(sK + tswz(4096, nt * 8 + rin, 4 * kp + mi), b0, b1, b2, b3);
-        mma_bf16_16816(sc[nt], qa[2 * kp], b0, b1);
-        mma_bf16_16816(sc[nt], qa[2 * kp + 1], b2, b3);
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t ka[4];
+        ldmatrix_x4(sK + tswz(4096, 16 * mt + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * kk + (lane >> 4)),
+                    ka[0], ka[1], ka[2], ka[3]);
+        mma_bf16_16816(sc[mt], ka, qb[kk][0], qb[kk][1]);
       }
     }
-    float mt = -INFINITY;
+    // online softmax per head column (its 32 tokens live in the 8 lanes
+    // that share tq: reduce over lane bits 2..4)
+    float cm[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
+    for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tok = nt * 8 + 2 * (lane & 3) + e;
-        const float v = tok < d.ntok ? sc[nt][e] * a.scale_log2 : -INFINITY;
-        sc[nt][e] = v;
-        mt = fmaxf(mt, v);
+      for (int i = 0; i < 4; ++i) {
+        const int tok = 16 * mt + g + 8 * (i >> 1);
+        const float v = tok < d.ntok ? sc[mt][i] * a.scale_log2 : -INFINITY;
+        sc[mt][i] = v;
+        cm[i & 1] = fmaxf(cm[i & 1], v);
       }
     }
-    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
-    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
-    const float m_new = fmaxf(m_run, mt);
-    const float alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - m_new);
-    m_run = m_new;
-    float ls = 0.f;
-    // P enters the PV MMA as bf16 hi + lo parts (hi = bf16(p), lo = bf16(p - hi)):
-    // ~16 significant bits of p instead of 8.
-    uint32_t ph2[2][4], pl[2][4];
+    float alpha[2], m_new[2];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const float p0 = m_new == -INFINITY ? 0.f : fast_exp2(sc[nt][0] - m_new);
-      const float p1 = m_new == -INFINITY ? 0.f : fast_exp2(sc[nt][1] - m_new);
-      ls += p0 + p1;
-      const uint32_t hk = pack_bf16x2(p0, p1);
-      const float2 hf = unpack_bf16x2(hk);
-      const uint32_t lk = pack_bf16x2(p0 - hf.x, p1 - hf.y);
-      const int kp = nt >> 1, hiw = (nt & 1) * 2;
-      ph2[kp][hiw] = hk; ph2[kp][hiw + 1] = 0u;
-      pl[kp][hiw] = lk; pl[kp][hiw + 1] = 0u;
+    for (int e = 0; e < 2; ++e) {
+      cm[e] = fmaxf(cm[e], __shfl_xor_sync(0xffffffffu, cm[e], 4));
+      cm[e] = fmaxf(cm[e], __shfl_xor_sync(0xffffffffu, cm[e], 8));
+      cm[e] = fmaxf(cm[e], __shfl_xor_sync(0xffffffffu, cm[e], 16));
+      m_new[e] = fmaxf(m_run[e], cm[e]);
+      alpha[e] = m_run[e] == -INFINITY ? 0.f : fast_exp2(m_run[e] - m_new[e]);
+      m_run[e] = m_new[e];
     }
-    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
-    l_run = l_run * alpha + ls;
+    // P (bf16, as the PV operand of the reference's flash attention) ->
+    // B fragments of P^T through 8x8 transposes
+    float ls[2] = {0.f, 0.f};
+    uint32_t pb[2][2];
 #pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      o[dt][0] *= alpha;
-      o[dt][1] *= alpha;
+    for (int mt = 0; mt < 2; ++mt) {
+      float pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        pv[i] = m_new[i & 1] == -INFINITY ? 0.f : fast_exp2(sc[mt][i] - m_new[i & 1]);
+        ls[i & 1] += pv[i];
+      }
+      pb[mt][0] = movmatrix_trans(pack_bf16x2(pv[0], pv[1]));  // tokens 16mt + 2tq, +1
+      pb[mt][1] = movmatrix_trans(pack_bf16x2(pv[2], pv[3]));  // tokens 16mt + 8 + 2tq, +1
     }
-    // O += P V (16 dim tiles of 8)
 #pragma unroll
-    for (int kp = 0; kp < 2; ++kp) {
+    for (int e = 0; e < 2; ++e) {
+      ls[e] += __shfl_xor_sync(0xffffffffu, ls[e], 4);
+      ls[e] += __shfl_xor_sync(0xffffffffu, ls[e], 8);
+      ls[e] += __shfl_xor_sync(0xffffffffu, ls[e], 16);
+      l_run[e] = l_run[e] * alpha[e] + ls[e];
+    }
 #pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        uint32_t v0, v1, v2, v3;
-        ldmatrix_x4_trans(sV + tswz(4096, kp * 16 + 8 * (mi & 1) + rin, 2 * dp + (mi >> 1)), v0, v1, v2, v3);
-        mma_bf16_16816(o[2 * dp], ph2[kp], v0, v1);
-        mma_bf16_16816(o[2 * dp + 1], ph2[kp], v2, v3);
-        mma_bf16_16816(o[2 * dp], pl[kp], v0, v1);
-        mma_bf16_16816(o[2 * dp + 1], pl[kp], v2, v3);
+    for (int md = 0; md < 8; ++md) {
+      ot[md][0] *= alpha[0]; ot[md][1] *= alpha[1];
+      ot[md][2] *= alpha[0]; ot[md][3] *= alpha[1];
+    }
+    // O^T += V^T P^T: 8 dim tiles x 2 token steps
+#pragma unroll
+    for (int md = 0; md < 8; ++md) {
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t va[4];
+        ldmatrix_x4_trans(sV + tswz(4096, 16 * ks + (lane & 7) + 8 * (lane >> 4), 2 * md + ((lane >> 3) & 1)),
+                          va[0], va[1], va[2], va[3]);
+        mma_bf16_16816(ot[md], va, pb[ks][0], pb[ks][1]);
       }
     }
 
     if (!d.last) continue;
     // ---- item done: output (single item) or partial + ticket
-    const int hq = d.h * a.G + g;
     if (d.npages == 1) {
-      if (live_row) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        __nv_bfloat16* dst = a.out + (size_t)d.qrow * a.out_stride + (size_t)hq * kDecHD;
+      // O / l, transposed back to [head][dim] rows: 4-byte stores of dim pairs
+      const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f;
+      const float inv1 = l_run[1] > 0.f ? 1.f / l_run[1] : 0.f;
+      // (the transposes are warp-wide: every lane runs them, then the lanes
+      // of the G live heads store)
+      __nv_bfloat16* dst = a.out + (size_t)d.qrow * a.out_stride + (size_t)(d.h * a.G + g) * kDecHD;
 #pragma unroll
-        for (int dt = 0; dt < 16; ++dt)
-          *reinterpret_cast<uint32_t*>(dst + dt * 8 + 2 * (lane & 3)) =
-              pack_bf16x2(o[dt][0] * inv, o[dt][1] * inv);
+      for (int md = 0; md < 8; ++md) {
+        const uint32_t lo = movmatrix_trans(pack_bf16x2(ot[md][0] * inv0, ot[md][1] * inv1));
+        const uint32_t hi = movmatrix_trans(pack_bf16x2(ot[md][2] * inv0, ot[md][3] * inv1));
+        if (g < a.G) {
+          *reinterpret_cast<uint32_t*>(dst + 16 * md + 2 * tq) = lo;
+          *reinterpret_cast<uint32_t*>(dst + 16 * md + 8 + 2 * tq) = hi;
+        }
       }
       continue;
     }
-    if (live_row) {
-      float* po = a.part_o + ((size_t)d.c * a.Hq + hq) * kDecHD;
 #pragma unroll
-      for (int dt = 0; dt < 16; ++dt)
-        *reinterpret_cast<float2*>(po + dt * 8 + 2 * (lane & 3)) = make_float2(o[dt][0], o[dt][1]);
-      if ((lane & 3) == 0)
-        *reinterpret_cast<float2*>(a.part_ml + ((size_t)d.c * a.Hq + hq) * 2) = make_float2(m_run, l_run);
+    for (int e = 0; e < 2; ++e) {
+      const int col = 2 * tq + e;
+      if (col < a.G) {
+        const size_t hq = (size_t)d.h * a.G + col;
+        float* po = a.part_o + ((size_t)d.c * a.Hq + hq) * kDecHD;
+#pragma unroll
+        for (int md = 0; md < 8; ++md) {
+          po[16 * md + g] = ot[md][e];
+          po[16 * md + 8 + g] = ot[md][2 + e];
+        }
+        if (g == 0)
+          *reinterpret_cast<float2*>(a.part_ml + ((size_t)d.c * a.Hq + hq) * 2) = make_float2(m_run[e], l_run[e]);
+      }
     }
     __threadfence();
     __syncwarp();
