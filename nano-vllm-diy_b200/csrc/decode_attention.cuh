@@ -190,6 +190,7 @@ __global__ void __launch_bounds__(128, 1)
   grab_item();
 
   int issued = 0, valid_issued = 0;
+  unsigned zeroed = 0;
   auto issue_next = [&]() {
     if (more) {
       const int s = issued % kDecStages;
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(128, 1)
         s_desc[s] = d;
         const uint32_t st = wsmem + s * kDecStageBytes;
         const uint32_t bar = smem_u32(&s_bar[s]);
-        fence_proxy_async_smem();
+        if (zeroed & (1u << s)) fence_proxy_async_smem();
         mbar_arrive_expect_tx(&s_bar[s], 4 * 4096 + (d.first ? 2 * 128 * a.q_box_rows : 0));
         const int r = (int)d.row;
         tma_load_3d(st + kDecStK, &tmK, bar, 0, d.h, r);
@@ -259,6 +260,9 @@ __global__ void __launch_bounds__(128, 1)
         *reinterpret_cast<uint4*>(vrow + tswz(4096, r, ch)) = make_uint4(0u, 0u, 0u, 0u);
       }
       __syncwarp();
+      zeroed |= 1u << s;
+    } else {
+      zeroed &= ~(1u << s);
     }
 
     if (d.first) {
