@@ -246,6 +246,25 @@ GemmPlan plan_gemm(DeviceState* ds, int T, int N, int K, bool silu_tiles) {
   return p;
 }
 
+// Decode attention: one CTA per SM, launched cooperatively (its merge phase
+// follows a grid-wide barrier, so every CTA must be resident).
+int launch_decode(DeviceState* ds, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                  const CUtensorMap& tmQ, const DecodeArgs& a, int smem, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ds->num_sms, 1, 1);
+  cfg.blockDim = dim3(kDecWarps * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_attn_kernel, tmK, tmV, tmQ, a);
+  if (e != cudaSuccess) return fail(B200_ERR_CUDA, "decode attention launch: %s", cudaGetErrorString(e));
+  return B200_OK;
+}
+
 // ---------------------------------------------------------------------------
 // SM-pair GEMM (gemm_pair_tcgen05_kernel): one CTA per SM, clusters (2, 1, S)
 // ---------------------------------------------------------------------------
@@ -807,7 +826,7 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
     a.err = ds->err;
     const int smem = dec_smem_bytes();
     if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
-    decode_attn_kernel<<<ds->num_sms, kDecWarps * 32, smem, st>>>(tmK, tmV, tmQ, a);
+    if (int r = launch_decode(ds, tmK, tmV, tmQ, a, smem, st)) return r;
     return check_launch("decode_attn_kernel");
   }
   PrefillArgs a{};
@@ -987,6 +1006,6 @@ extern "C" int b200_paged_decode_attention_static(
   a.err = ds->err;
   const int smem = dec_smem_bytes();
   if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
-  decode_attn_kernel<<<ds->num_sms, kDecWarps * 32, smem, st>>>(tmK, tmV, tmQ, a);
+  if (int r = launch_decode(ds, tmK, tmV, tmQ, a, smem, st)) return r;
   return check_launch("decode_attn_kernel");
 }

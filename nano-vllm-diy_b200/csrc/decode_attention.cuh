@@ -70,6 +70,12 @@ struct DecTile {
   long long row;  // cache row (slot) of the tile's first token
 };
 
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __host__ __device__ constexpr int dec_smem_bytes() {
   return 1024 + kDecWarps * kDecWarpBytes + kDecWarps * kDecStages * 8 +
          kDecWarps * kDecStages * (int)sizeof(DecTile) + (8 + kDecMaxSeqs + 1) * (int)sizeof(int);
@@ -388,62 +394,6 @@ __global__ void __launch_bounds__(128, 1)
           *reinterpret_cast<float2*>(a.part_ml + ((size_t)d.c * a.Hq + hq) * 2) = make_float2(m_run[e], l_run[e]);
       }
     }
-    __threadfence();
-    __syncwarp();
-    int ticket = 0;
-    if (lane == 0) ticket = atomicAdd(a.tickets + (size_t)d.b * a.Hkv + d.h, 1);
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
-    if (ticket != d.npages - 1) continue;
-    __threadfence();
-    // this warp merges the npages partials of (b, h): every lane loads the
-    // (m, l) of one item at a time and the partial rows are read 8 items per
-    // batch, so the merge is not a chain of dependent L2 round trips
-    const int c0 = s_start[d.b];
-    const int np = d.npages;
-    for (int gg = 0; gg < a.G; ++gg) {
-      const size_t hqq = (size_t)d.h * a.G + gg;
-      float M = -INFINITY;
-      for (int p0 = 0; p0 < np; p0 += 32) {
-        if (p0 + lane < np) M = fmaxf(M, __ldcg(a.part_ml + ((size_t)(c0 + p0 + lane) * a.Hq + hqq) * 2));
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-      float L = 0.f;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p0 = 0; p0 < np; p0 += 32) {
-        float w = 0.f;
-        if (p0 + lane < np) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + ((size_t)(c0 + p0 + lane) * a.Hq + hqq) * 2));
-          w = fast_exp2(ml.x - M);
-          L += w * ml.y;
-        }
-        const int cnt = min(32, np - p0);
-        for (int j = 0; j < cnt; j += 8) {
-          float4 ov[8];
-          float wj[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            wj[u] = __shfl_sync(0xffffffffu, w, j + u);
-            ov[u] = j + u < cnt
-                        ? __ldcg(reinterpret_cast<const float4*>(a.part_o + ((size_t)(c0 + p0 + j + u) * a.Hq + hqq) * kDecHD) + lane)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            acc.x += wj[u] * ov[u].x; acc.y += wj[u] * ov[u].y;
-            acc.z += wj[u] * ov[u].z; acc.w += wj[u] * ov[u].w;
-          }
-        }
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-      uint2 packed;
-      packed.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-      packed.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-      *reinterpret_cast<uint2*>(a.out + (size_t)d.qrow * a.out_stride + hqq * kDecHD + lane * 4) = packed;
-    }
-    if (lane == 0) atomicExch(a.tickets + (size_t)d.b * a.Hkv + d.h, 0);
   }
   // drain: every issued tile has landed before the CTA's shared memory is released
   if (lane == 0) {
@@ -451,6 +401,99 @@ __global__ void __launch_bounds__(128, 1)
       mbar_wait(&s_bar[t % kDecStages], (uint32_t)(t / kDecStages) & 1u, a.err);
   }
   __syncwarp();
+
+  // ---- grid barrier: every warp's partials are written (the launch is
+  // cooperative, so all CTAs are resident; the wait is bounded)
+  if (lane == 0) {
+    __threadfence();
+    atomicAdd(&sched[2], 1);
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_gpu_s32(&sched[2]) < nwarps) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        raise_error(a.err, ERR_PEER_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+
+  // ---- merge phase: (sequence, kv head) units of sequences split into
+  // several items, taken from a queue by every warp.  Each lane owns 4 of the
+  // 128 dims of every head of the group; loads are batched over items and
+  // heads so a merge costs a few memory round trips.
+  const int units = a.B * a.Hkv;
+  while (true) {
+    int u = 0;
+    if (lane == 0) u = atomicAdd(&sched[3], 1);
+    u = __shfl_sync(0xffffffffu, u, 0);
+    if (u >= units) break;
+    const int b = u / a.Hkv, h = u - b * a.Hkv;
+    const int c0 = s_start[b], np = s_start[b + 1] - c0;
+    if (np <= 1) continue;  // written directly (or an empty row)
+    const int G = a.G;
+    float M[8], L[8];
+    float4 acc[8];
+#pragma unroll
+    for (int gg = 0; gg < 8; ++gg) {
+      M[gg] = -INFINITY;
+      L[gg] = 0.f;
+      acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // pass 1: the maxima, lanes over items
+    for (int p0 = 0; p0 < np; p0 += 32) {
+      const int pp = p0 + lane;
+#pragma unroll
+      for (int gg = 0; gg < 8; ++gg)
+        if (gg < G && pp < np)
+          M[gg] = fmaxf(M[gg], __ldcg(a.part_ml + ((size_t)(c0 + pp) * a.Hq + (size_t)h * G + gg) * 2));
+    }
+#pragma unroll
+    for (int gg = 0; gg < 8; ++gg)
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M[gg] = fmaxf(M[gg], __shfl_xor_sync(0xffffffffu, M[gg], off));
+    // pass 2: weighted sums, 2 items x every head per batch of loads
+    for (int p0 = 0; p0 < np; p0 += 2) {
+      float2 ml[2][8];
+      float4 ov[2][8];
+#pragma unroll
+      for (int uu = 0; uu < 2; ++uu)
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) {
+          const bool live = gg < G && p0 + uu < np;
+          const size_t row = (size_t)(c0 + p0 + uu) * a.Hq + (size_t)h * G + gg;
+          ml[uu][gg] = live ? __ldcg(reinterpret_cast<const float2*>(a.part_ml + row * 2))
+                            : make_float2(-INFINITY, 0.f);
+          ov[uu][gg] = live ? __ldcg(reinterpret_cast<const float4*>(a.part_o + row * kDecHD) + lane)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int uu = 0; uu < 2; ++uu)
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) {
+          const float w = ml[uu][gg].x == -INFINITY ? 0.f : fast_exp2(ml[uu][gg].x - M[gg]);
+          L[gg] += w * ml[uu][gg].y;
+          acc[gg].x += w * ov[uu][gg].x; acc[gg].y += w * ov[uu][gg].y;
+          acc[gg].z += w * ov[uu][gg].z; acc[gg].w += w * ov[uu][gg].w;
+        }
+    }
+    const int qrow = a.cu_q[b];
+#pragma unroll
+    for (int gg = 0; gg < 8; ++gg) {
+      if (gg >= G) continue;
+      const float inv = L[gg] > 0.f ? 1.f / L[gg] : 0.f;
+      uint2 packed;
+      packed.x = pack_bf16x2(acc[gg].x * inv, acc[gg].y * inv);
+      packed.y = pack_bf16x2(acc[gg].z * inv, acc[gg].w * inv);
+      *reinterpret_cast<uint2*>(a.out + (size_t)qrow * a.out_stride + ((size_t)h * G + gg) * kDecHD + lane * 4) =
+          packed;
+    }
+  }
+  // the last warp out resets the merge queue and the barrier for the next call
+  if (lane == 0 && atomicAdd(&sched[4], 1) == nwarps - 1) {
+    atomicExch(&sched[2], 0);
+    atomicExch(&sched[3], 0);
+    atomicExch(&sched[4], 0);
+  }
 }
 
 }  // namespace b200
