@@ -796,7 +796,7 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
   const int G = Hq / Hkv;
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   if (max_seqlen_q == 1 && block_tables && G <= 8 && B <= kDecMaxSeqs && Hkv <= kDecMaxKvHeads &&
-      page % kDecItem == 0) {
+      page % 256 == 0) {
     if (!workspace || ws_bytes <= (size_t)kDecTicketBytes || !aligned16(workspace))
       return fail(B200_ERR_WORKSPACE, "attention: decode workspace missing or too small");
     if (num_q_rows <= 0) return fail(B200_ERR_INVALID, "attention: num_q_rows must be positive");
@@ -959,8 +959,8 @@ extern "C" int b200_paged_decode_attention_static(
                 "decode_static: needs Hq %% Hkv == 0, Hq/Hkv <= 8, Hkv <= %d, B <= %d", kDecMaxKvHeads,
                 kDecMaxSeqs);
   if (!q || !k_cache || !v_cache || !block_tables || !cu_seqlens_q || !cu_seqlens_k || !out ||
-      page <= 0 || page % kDecItem || num_q_rows <= 0 || max_seqlen_k < 0)
-    return fail(B200_ERR_INVALID, "decode_static: missing argument or page not a multiple of %d", kDecItem);
+      page <= 0 || page % 256 || num_q_rows <= 0 || max_seqlen_k < 0)
+    return fail(B200_ERR_INVALID, "decode_static: missing argument or page not a multiple of 256");
   if (q_stride % 8 || out_stride % 8 || !aligned16(q) || !aligned16(out) || !aligned16(k_cache) ||
       !aligned16(v_cache))
     return fail(B200_ERR_INVALID, "decode_static: rows must be 16-byte aligned");

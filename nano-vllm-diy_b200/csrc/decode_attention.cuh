@@ -6,22 +6,22 @@
 // cached key is visible), GQA (q head n reads kv head n / G).
 //
 // Work decomposition (HBM-bound: every K/V byte is read exactly once):
-//   item  = (256-token group of one sequence, kv head).  256 divides the
-//           reference's block size (runner_config.py:39), so an item lies in
-//           one physical block.  The G = Hq / Hkv query heads that share the
-//           kv head are the rows of one m16n8k16 MMA.
+//   item  = (512-token group of one sequence, kv head); an item may span
+//           pages (their block-table entries are read once per item).  The
+//           G = Hq / Hkv query heads that share the kv head are the columns
+//           of the MMAs (tokens are the rows: S^T = K Q^T, O^T = V^T P^T).
 //   warp  = owns whole items, taken from a global atomic counter (dynamic
 //           scheduling: no tail from uneven sequence lengths).  Each warp
 //           runs its own 3-stage ring of 32-token K/V tiles (+ the item's Q
 //           rows with its first tile) loaded by TMA (cp.async.bulk.tensor,
 //           128-byte swizzle, one mbarrier per stage, issued by lane 0), so
 //           the ring keeps streaming across item boundaries and no CTA-wide
-//           barrier is taken after the start.
-//   merge = a sequence spanning several items writes per-item partials
-//           (m, l, o); the warp that finishes the last item of (sequence,
-//           kv head) -- found with an atomic ticket -- merges them and writes
-//           the output, then resets the ticket.  A single-item sequence
-//           writes its output directly.
+//           barrier is taken in the main loop.
+//   merge = a sequence spanning several items writes per-item fp32 partials
+//           (m, l, o) with plain stores; after a grid-wide barrier (the
+//           launch is cooperative, so every CTA is resident) all warps take
+//           the split (sequence, kv head) pairs from a second queue and merge
+//           them.  A single-item sequence writes its output directly.
 // The launch shape depends only on the SM count; context lengths are read
 // from cu_seqlens_k on the device (CUDA-graph safe; rows with q length <= 0
 // are graph padding and are skipped).
@@ -31,7 +31,8 @@
 namespace b200 {
 
 constexpr int kDecHD = 128;
-constexpr int kDecItem = 256;     // tokens per work item
+constexpr int kDecItem = 512;     // tokens per work item (may span pages)
+constexpr int kDecItemPages = 4;  // block-table entries an item can touch (pages >= 256 tokens)
 constexpr int kDecTile = 32;      // tokens per pipeline stage
 constexpr int kDecStages = 3;
 constexpr int kDecWarps = 4;
@@ -65,9 +66,10 @@ struct DecodeArgs {
 
 struct DecTile {
   int b, h, c, npages, qrow;
-  int ntok;     // valid tokens in the tile
+  int ntok;     // valid tokens in the tile (the item's, in the iterator)
   int first, last;
   long long row;  // cache row (slot) of the tile's first token
+  int j0;         // iterator: the item's first token in the sequence
 };
 
 __device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
@@ -157,6 +159,7 @@ __global__ void __launch_bounds__(128, 1)
   bool more = true;       // the warp may still take items
   int it_k = 0, it_tiles = 0;
   DecTile cur{};
+  long long blk0 = -1, blk1 = -1, blk2 = -1, blk3 = -1;  // the current item's pages
   auto grab_item = [&]() {
     int w = 0;
     if (lane == 0) w = atomicAdd(&sched[0], 1);
@@ -181,15 +184,20 @@ __global__ void __launch_bounds__(128, 1)
     const int j0 = (c - s_start[b]) * kDecItem;
     const int nk = a.cu_k[b + 1] - a.cu_k[b];
     const int ntok_item = min(kDecItem, nk - j0);
-    const int col = j0 / a.page;
-    const long long blk = col < a.bt_width ? a.block_tables[(size_t)b * a.bt_stride + col] : -1;
-    const long long row = blk * a.page + (j0 % a.page);
+    // the block-table entries of the item's pages (one per lane 0..3)
+    const int col0 = j0 / a.page;
+    long long e = -1;
+    if (lane < kDecItemPages && col0 + lane < a.bt_width)
+      e = a.block_tables[(size_t)b * a.bt_stride + col0 + lane];
+    blk0 = __shfl_sync(0xffffffffu, e, 0);
+    blk1 = __shfl_sync(0xffffffffu, e, 1);
+    blk2 = __shfl_sync(0xffffffffu, e, 2);
+    blk3 = __shfl_sync(0xffffffffu, e, 3);
     cur.b = b; cur.h = h; cur.c = c;
     cur.npages = s_start[b + 1] - s_start[b];
     cur.qrow = a.cu_q[b];
     cur.ntok = ntok_item;
-    cur.row = (blk < 0 || row + ntok_item > a.num_slots) ? -1 : row;
-    if (cur.row < 0 && lane == 0) raise_error(a.err, ERR_BAD_INDEX);
+    cur.j0 = j0;
     it_tiles = (ntok_item + kDecTile - 1) / kDecTile;
     it_k = 0;
   };
@@ -201,11 +209,19 @@ __global__ void __launch_bounds__(128, 1)
     if (more) {
       const int s = issued % kDecStages;
       DecTile d = cur;
-      // an invalid block loads rows 0.. of the cache and masks every token
-      d.ntok = cur.row < 0 ? 0 : min(kDecTile, cur.ntok - it_k * kDecTile);
+      // the tile's page and cache row; an invalid block loads rows 0.. of
+      // the cache and masks every token
+      const int tok0 = cur.j0 + it_k * kDecTile;
+      const int pi = tok0 / a.page - cur.j0 / a.page;
+      const long long blk = pi == 0 ? blk0 : pi == 1 ? blk1 : pi == 2 ? blk2 : pi == 3 ? blk3 : -1;
+      const int ntile = min(kDecTile, cur.ntok - it_k * kDecTile);
+      const long long row = blk * a.page + (tok0 % a.page);
+      const bool valid = blk >= 0 && row + ntile <= a.num_slots;
+      if (!valid && lane == 0) raise_error(a.err, ERR_BAD_INDEX);
+      d.ntok = valid ? ntile : 0;
       d.first = it_k == 0;
       d.last = it_k == it_tiles - 1;
-      d.row = cur.row < 0 ? 0 : cur.row + (long long)it_k * kDecTile;
+      d.row = valid ? row : 0;
       if (lane == 0) {
         s_desc[s] = d;
         const uint32_t st = wsmem + s * kDecStageBytes;
