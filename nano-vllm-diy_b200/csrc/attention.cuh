@@ -58,6 +58,8 @@ constexpr int kPfBM = 64;  // queries per CTA
 constexpr int kPfBN = 64;  // keys per tile
 
 __global__ void __launch_bounds__(128) prefill_attn_kernel(const PrefillArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sQ = smem;                    // 64 x 256 B
   uint8_t* sK = smem + 16384;            // 2 stages x 64 x 256 B

@@ -61,6 +61,20 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A grid launched with programmatic stream
+// serialization may start while the previous grid of its stream is still
+// running; griddep_wait() blocks until that grid has completed and its memory
+// operations are visible (a no-op for a normally launched grid), and
+// griddep_launch_dependents() lets the next grid start launching.  Every
+// kernel of this library waits before it reads data a previous kernel may
+// have written, so completion stays ordered along the stream.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

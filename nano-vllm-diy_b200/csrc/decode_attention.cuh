@@ -114,6 +114,10 @@ __global__ void __launch_bounds__(128, 1)
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmQ);
   }
+  // the barrier setup above overlaps the previous kernel's tail
+  // (programmatic dependent launch); sequence lengths, Q and the cache below
+  griddep_wait();
+  griddep_launch_dependents();
 
   // ---- plan: exclusive prefix sum of items per sequence (identical in every CTA)
   {

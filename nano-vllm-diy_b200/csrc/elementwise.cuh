@@ -28,6 +28,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
                                                        long long out_stride,
                                                        __nv_bfloat16* __restrict__ res_out,
                                                        int dim, float eps) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float s_red[8];
   const int row = blockIdx.x;
   const int nvec = dim / 8;
@@ -123,6 +125,8 @@ struct QKNormRopeArgs {
 };
 
 __global__ void __launch_bounds__(256) qk_norm_rope_store_kernel(const QKNormRopeArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int heads = a.Hq + (a.v_in ? 2 : 1) * a.Hkv;
@@ -218,6 +222,8 @@ __global__ void store_kvcache_kernel(const __nv_bfloat16* __restrict__ key, long
                                      __nv_bfloat16* __restrict__ v_cache,
                                      const int* __restrict__ slot_mapping, int T, int D,
                                      long long num_slots, unsigned* err) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int vpt = D / 8;  // 16-byte vectors per token row
   const long long total = (long long)T * vpt;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -243,6 +249,8 @@ __global__ void store_kvcache_kernel(const __nv_bfloat16* __restrict__ key, long
 __global__ void silu_and_mul_kernel(const __nv_bfloat16* __restrict__ x, long long x_stride,
                                     __nv_bfloat16* __restrict__ out, long long out_stride, int T,
                                     int I) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int vpr = I / 8;
   const long long total = (long long)T * vpr;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -274,6 +282,8 @@ __global__ void silu_and_mul_kernel(const __nv_bfloat16* __restrict__ x, long lo
 __global__ void embedding_kernel(const long long* __restrict__ ids,
                                  const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                  int T, int H, long long start, long long end, unsigned* err) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int vpr = H / 8;
   const long long total = (long long)T * vpr;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -294,6 +304,8 @@ __global__ void embedding_kernel(const long long* __restrict__ ids,
 __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* __restrict__ logits,
                                                       long long stride, int V,
                                                       long long* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float s_v[32];
   __shared__ int s_i[32];
   const int row = blockIdx.x;

@@ -377,6 +377,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above overlaps the previous kernel's tail (programmatic
+  // dependent launch); activations and peer buffers are read below
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {

@@ -237,6 +237,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // both CTAs' barriers initialised before either signals the other
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above overlaps the previous kernel's tail (programmatic
+  // dependent launch); activations and the stream-K workspace are used below
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ---- producer (both CTAs): this CTA's 128 tokens and NP/2 weight rows
