@@ -196,8 +196,8 @@ int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_
  *    with q length <= 0 (CUDA-graph padding) are skipped.
  *  - max_seqlen_q == 1 with a block table (B <= 1024, Hkv <= 64, Hq/Hkv <= 8,
  *    page a multiple of 256) takes the split-KV decode kernel and needs
- *    `workspace` (b200_attention_workspace_bytes).  Its first 256 KiB + 256
- *    bytes hold work-queue and barrier counters that must be zero before the
+ *    `workspace` (b200_attention_workspace_bytes).  Its first 256 bytes hold
+ *    work-queue and barrier counters that must be zero before the
  *    first call and are zero again after every call; the rest is per-call
  *    scratch (split-KV partials).  The kernel is launched cooperatively (a
  *    grid-wide barrier precedes its merge phase).  Calls that share a
@@ -220,8 +220,8 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
  * loops that must not call cudaMalloc (it may synchronise the device and
  * cannot be recorded into a CUDA graph).
  *  - Limits: B <= 1024, Hkv <= 64, Hq / Hkv <= 8, page a multiple of 256, and
- *    256 KiB + B * ceil(max_seqlen_k / 512) * Hq * 520 bytes must fit the
- *    32 MiB array (e.g. 240 sequences of 4096 keys with 32 heads); larger
+ *    256 + B * ceil(max_seqlen_k / 512) * Hq * 520 bytes must fit the
+ *    32 MiB array (e.g. 252 sequences of 4096 keys with 32 heads); larger
  *    problems return B200_ERR_WORKSPACE without launching anything.
  *  - The first call on a device looks up the array's device address; make
  *    that first call before any CUDA-graph capture.

@@ -825,7 +825,7 @@ int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_
   if (!bytes || max_seqs < 0 || max_seqlen_k < 0 || Hq <= 0)
     return fail(B200_ERR_INVALID, "bad arguments");
   const size_t items = (size_t)max_seqs * ((max_seqlen_k + kDecItem - 1) / kDecItem);
-  *bytes = (size_t)kDecTicketBytes + items * Hq * (kDecHD + 2) * sizeof(float);
+  *bytes = (size_t)kDecSchedBytes + items * Hq * (kDecHD + 2) * sizeof(float);
   return B200_OK;
 }
 
@@ -852,7 +852,7 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
   const float scale_log2 = softmax_scale * 1.4426950408889634f;
   if (max_seqlen_q == 1 && block_tables && G <= 8 && B <= kDecMaxSeqs && Hkv <= kDecMaxKvHeads &&
       page % 256 == 0) {
-    if (!workspace || ws_bytes <= (size_t)kDecTicketBytes || !aligned16(workspace))
+    if (!workspace || ws_bytes <= (size_t)kDecSchedBytes || !aligned16(workspace))
       return fail(B200_ERR_WORKSPACE, "attention: decode workspace missing or too small");
     if (num_q_rows <= 0) return fail(B200_ERR_INVALID, "attention: num_q_rows must be positive");
     const size_t per_item = (size_t)Hq * (kDecHD + 2) * sizeof(float);
@@ -873,9 +873,9 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
     a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = G; a.page = page; a.q_box_rows = qbox;
     a.num_slots = num_slots;
     a.scale_log2 = scale_log2;
-    a.tickets = static_cast<int*>(workspace);
-    a.cap_items = (long long)((ws_bytes - kDecTicketBytes) / per_item);
-    a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + kDecTicketBytes);
+    a.sched = static_cast<int*>(workspace);
+    a.cap_items = (long long)((ws_bytes - kDecSchedBytes) / per_item);
+    a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + kDecSchedBytes);
     a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
     a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
     a.err = ds->err;
@@ -972,8 +972,7 @@ int b200_linear_allreduce(const void* x, long long ldx, const void* w, long long
 // that must never call cudaMalloc -- cudaMalloc can synchronise the device
 // and stall every stream, and it cannot be recorded into a CUDA graph.  For
 // them b200_paged_decode_attention_static keeps the decode kernel's scratch
-// (per-(sequence, kv head) tickets, the work counter and the split-KV
-// partials) in the fixed array below.  The array is part of the library
+// (the scheduler counters and the split-KV partials) in the fixed array below.  The array is part of the library
 // image: every GPU that loads libb200ops.so holds these 32 MiB until the
 // process exits.
 // ===========================================================================
@@ -1021,7 +1020,7 @@ extern "C" int b200_paged_decode_attention_static(
     return fail(B200_ERR_INVALID, "decode_static: rows must be 16-byte aligned");
   const size_t per_item = (size_t)Hq * (kDecHD + 2) * sizeof(float);
   const size_t items = (size_t)B * ((max_seqlen_k + kDecItem - 1) / kDecItem);
-  const size_t need = (size_t)kDecTicketBytes + items * per_item;
+  const size_t need = (size_t)kDecSchedBytes + items * per_item;
   if (need > kStaticDecodeScratchBytes)
     return fail(B200_ERR_WORKSPACE,
                 "decode_static: %d sequences of up to %d keys with %d heads need %zu bytes of scratch; "
@@ -1032,9 +1031,9 @@ extern "C" int b200_paged_decode_attention_static(
   void* scratch = nullptr;
   if (int r = static_decode_scratch(&scratch)) return r;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // the tickets and the work counter must start at zero; a call that ended
-  // early must not leave stale counts for this one
-  cudaError_t e = cudaMemsetAsync(scratch, 0, kDecTicketBytes, st);
+  // the scheduler counters must start at zero; a call that ended early must
+  // not leave stale counts for this one
+  cudaError_t e = cudaMemsetAsync(scratch, 0, kDecSchedBytes, st);
   if (e != cudaSuccess) return fail(B200_ERR_CUDA, "decode_static: clear: %s", cudaGetErrorString(e));
   CUtensorMap tmK, tmV, tmQ;
   const int qbox = Hq < 8 ? Hq : 8;
@@ -1053,9 +1052,9 @@ extern "C" int b200_paged_decode_attention_static(
   a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.G = Hq / Hkv; a.page = page; a.q_box_rows = qbox;
   a.num_slots = num_slots;
   a.scale_log2 = softmax_scale * 1.4426950408889634f;
-  a.tickets = static_cast<int*>(scratch);
-  a.cap_items = (long long)((kStaticDecodeScratchBytes - kDecTicketBytes) / per_item);
-  a.part_ml = reinterpret_cast<float*>(static_cast<char*>(scratch) + kDecTicketBytes);
+  a.sched = static_cast<int*>(scratch);
+  a.cap_items = (long long)((kStaticDecodeScratchBytes - kDecSchedBytes) / per_item);
+  a.part_ml = reinterpret_cast<float*>(static_cast<char*>(scratch) + kDecSchedBytes);
   a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
   a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
   a.err = ds->err;

@@ -36,16 +36,16 @@ constexpr int kDecItemPages = 4;  // block-table entries an item can touch (page
 constexpr int kDecTile = 32;      // tokens per pipeline stage
 constexpr int kDecStages = 3;
 constexpr int kDecWarps = 4;
-constexpr int kDecMaxSeqs = 1024;       // plan / ticket capacity
+constexpr int kDecMaxSeqs = 1024;       // plan capacity (prefix sums in shared memory)
 constexpr int kDecMaxKvHeads = 64;
 // stage: K [2 halves][32 rows][128 B] | V same | Q [2 halves][8 rows][128 B]
 constexpr int kDecStK = 0, kDecStV = 8192, kDecStQ = 16384;
 constexpr int kDecStageBytes = 18432;
 constexpr int kDecWarpBytes = kDecStages * kDecStageBytes;
-// workspace head: tickets [kDecMaxSeqs * kDecMaxKvHeads] ints, then the
-// scheduler words {next item, warps done}; all zero between calls
-constexpr int kDecSchedOffset = kDecMaxSeqs * kDecMaxKvHeads * 4;
-constexpr int kDecTicketBytes = kDecSchedOffset + 256;
+// workspace head: the scheduler words {next item, warps done, warps at the
+// grid barrier, next merge unit, warps merged}; zero between calls (the last
+// warp of each phase resets them)
+constexpr int kDecSchedBytes = 256;
 
 struct DecodeArgs {
   const int* block_tables;
@@ -55,7 +55,7 @@ struct DecodeArgs {
   int B, Hq, Hkv, G, page, q_box_rows;
   long long num_slots;
   float scale_log2;      // softmax_scale * log2(e)
-  int* tickets;          // workspace head (see kDecTicketBytes)
+  int* sched;            // workspace head (kDecSchedBytes)
   float* part_ml;        // [cap_items][Hq][2]
   float* part_o;         // [cap_items][Hq][128]
   long long cap_items;
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(128, 1)
   int* s_scan = reinterpret_cast<int*>(smem + kDecWarps * kDecWarpBytes + kDecWarps * kDecStages * 8 +
                                        kDecWarps * kDecStages * sizeof(DecTile));
   int* s_start = s_scan + 8;
-  int* sched = a.tickets + kDecSchedOffset / 4;   // {next item, warps done}
+  int* sched = a.sched;
 
   if (lane == 0) {
     for (int i = 0; i < kDecStages; ++i) mbar_init(&s_bar[i], 1);
@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(128, 1)
     }
 
     if (!d.last) continue;
-    // ---- item done: output (single item) or partial + ticket
+    // ---- item done: output (single item) or split-KV partial
     if (d.npages == 1) {
       // O / l, transposed back to [head][dim] rows: 4-byte stores of dim pairs
       const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f;

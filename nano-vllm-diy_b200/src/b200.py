@@ -6,10 +6,10 @@ include/b200ops.h and raises RuntimeError on a non-zero status.  There is no
 fallback: if the shared library is missing or a tensor is not on a CUDA
 device, the call fails.
 
-The decode-attention workspace (split-KV partials and its scheduling
-tickets) is a per-device torch buffer that grows on demand outside CUDA-graph
-capture and is reused by every call; the GEMMs need none (split-K partials
-are reduced in cluster shared memory).
+The decode-attention workspace (its scheduler counters and split-KV partials)
+and the GEMM workspace (stream-K flags and fp32 partials of the SM-pair GEMM)
+are per-device torch buffers that grow on demand outside CUDA-graph capture
+and are reused by every call.
 """
 from __future__ import annotations
 
@@ -137,9 +137,9 @@ _workspaces: dict[tuple[int, str], torch.Tensor] = {}
 
 
 def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
-    """Zero-filled on (re)allocation: the attention workspace starts with the
-    per-(sequence, kv head) tickets of the fused decode combine, which must be
-    zero before the first call (every call leaves them zero)."""
+    """Zero-filled on (re)allocation: both workspaces start with counters or
+    flags that must be zero before the first call (every call leaves them
+    zero)."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), kind)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:

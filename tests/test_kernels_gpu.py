@@ -280,7 +280,7 @@ def test_decode_attention_paged(Hq, Hkv):
 
 def test_decode_attention_long_and_repeated():
     """Sequences of > 32 items (the merge loops in rounds) and two calls in a
-    row (the per-sequence tickets of the fused merge must reset)."""
+    row (the scheduler counters of the merge phase must reset)."""
     from src import b200
     lens_k = [9000, 8193, 256, 511, 33]
     q, kc, vc, bt, cu_q, cu_k = _paged_case([1] * 5, lens_k, 32, 8, seed=31)
