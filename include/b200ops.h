@@ -57,11 +57,21 @@ int b200_device_error(unsigned* out, int clear);
  * Linear layers
  * ------------------------------------------------------------------------ */
 
-/* Workspace bytes b200_linear / b200_linear_silu_and_mul use: the stream-K
+/* Workspace bytes b200_linear / b200_linear_silu_and_mul use: the split-K
  * flags and fp32 partial tiles of the persistent SM-pair GEMM (4 KiB +
  * 128 KiB per SM, the same for every shape).  The workspace must be
  * zero-filled before its first use; every call leaves it reusable. */
 int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes);
+
+/* Host-side check of the SM-pair GEMM's work split (no counterpart in the
+ * reference; no CUDA call): plans `tiles` output tiles of `num_kb` 64-wide K
+ * blocks over at most `max_pairs` SM pairs (grouped schedule allowed when
+ * `grouped` is non-zero), walks every pair's segments with the iterator the
+ * kernel uses, and returns the number of violations: (tile, K block) units
+ * not covered exactly once, malformed segments, group members out of place,
+ * flag words outside the workspace's flag area.  0 = the schedule partitions
+ * the work.  Negative status on bad arguments. */
+int b200_gemm_schedule_check(long long tiles, int num_kb, int max_pairs, int grouped);
 
 /* y[T, N] = x[T, K] * w[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate,
  * tcgen05 tensor cores.  Replaces F.linear in
@@ -71,8 +81,9 @@ int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes);
  * K, ldx and ldw must be multiples of 8; x and w 16-byte aligned.
  * With a workspace of b200_linear_workspace_bytes() bytes (zeroed once,
  * 16-byte aligned) the GEMM runs on the persistent SM-pair kernel
- * (tcgen05.mma.cta_group::2, stream-K); with NULL it runs on the single-SM
- * kernel.  Concurrent calls must not share one workspace. */
+ * (tcgen05.mma.cta_group::2; grouped split-K or stream-K schedule) where
+ * that is faster; with NULL it runs on the single-SM kernel.  Concurrent
+ * calls must not share one workspace. */
 int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
                 void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
                 b200_stream_t stream);
@@ -196,11 +207,12 @@ int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_
  *    with q length <= 0 (CUDA-graph padding) are skipped.
  *  - max_seqlen_q == 1 with a block table (B <= 1024, Hkv <= 64, Hq/Hkv <= 8,
  *    page a multiple of 256) takes the split-KV decode kernel and needs
- *    `workspace` (b200_attention_workspace_bytes).  Its first 256 bytes hold
- *    work-queue and barrier counters that must be zero before the
- *    first call and are zero again after every call; the rest is per-call
- *    scratch (split-KV partials).  The kernel is launched cooperatively (a
- *    grid-wide barrier precedes its merge phase).  Calls that share a
+ *    `workspace` (b200_attention_workspace_bytes).  Its first 256 KiB + 256
+ *    bytes hold work-queue words and per-(sequence, kv head) completion
+ *    counters that must be zero before the first call and are zero again
+ *    after every call; the rest is per-call scratch (split-KV partials).  The
+ *    kernel is launched cooperatively (its merges wait, bounded, on items
+ *    that other CTAs compute).  Calls that share a
  *    workspace must not overlap on the GPU. */
 int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, const void* k,
                          long long k_stride,
@@ -220,8 +232,8 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
  * loops that must not call cudaMalloc (it may synchronise the device and
  * cannot be recorded into a CUDA graph).
  *  - Limits: B <= 1024, Hkv <= 64, Hq / Hkv <= 8, page a multiple of 256, and
- *    256 + B * ceil(max_seqlen_k / 512) * Hq * 520 bytes must fit the
- *    32 MiB array (e.g. 252 sequences of 4096 keys with 32 heads); larger
+ *    256 KiB + 256 + B * ceil(max_seqlen_k / 512) * Hq * 520 bytes must fit the
+ *    32 MiB array (e.g. 250 sequences of 4096 keys with 32 heads); larger
  *    problems return B200_ERR_WORKSPACE without launching anything.
  *  - The first call on a device looks up the array's device address; make
  *    that first call before any CUDA-graph capture.

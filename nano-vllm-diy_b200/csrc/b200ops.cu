@@ -221,6 +221,8 @@ int make_tmap_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
 // ---------------------------------------------------------------------------
 struct GemmPlan {
   int BN, token_tiles, n_tiles, num_kb, kb_per_split, splits, stages, smem, tmem_cols;
+  // SM-pair kernel schedule (GemmArgs::sched, grp_*)
+  int sched, grp_whole, grp_split, grp_size;
 };
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -299,13 +301,14 @@ int launch_decode(DeviceState* ds, const CUtensorMap& tmK, const CUtensorMap& tm
 }
 
 // ---------------------------------------------------------------------------
-// SM-pair GEMM (gemm_pair_tcgen05_kernel): one CTA per SM, clusters (2, 1, S)
+// SM-pair GEMM (gemm_pair_tcgen05_kernel): one CTA per SM, clusters of 2
 // ---------------------------------------------------------------------------
 constexpr int kPairSmemBudget = 226 * 1024;  // one CTA per SM (227 KB opt-in limit)
 
 // B200_GEMM_PAIR=0 selects the single-SM kernel for every shape and
-// B200_GEMM_PAIR=2 the SM-pair kernel for every shape (read at every call, so
-// a process can compare the two kernels).
+// B200_GEMM_PAIR=2 the SM-pair kernel for every shape; B200_GEMM_SCHED=
+// streamk keeps the SM-pair kernel on its stream-K schedule.  Read at every
+// call, so a process can compare the kernels and schedules.
 bool pair_enabled() {
   const char* e = getenv("B200_GEMM_PAIR");
   return !(e && *e == '0');
@@ -314,9 +317,43 @@ bool pair_forced() {
   const char* e = getenv("B200_GEMM_PAIR");
   return e && *e == '2';
 }
+bool grouped_allowed() {
+  const char* e = getenv("B200_GEMM_SCHED");
+  return !(e && std::strcmp(e, "streamk") == 0);
+}
 
-// Co-resident CTAs of the pair kernel with clusters of (2, 1, splits) and the
-// given dynamic shared memory (occupancy queries are slow: cached).
+struct PairSchedule {
+  int sched, pairs, whole, split, group;
+};
+
+// Work split of the SM-pair kernel over at most `max_pairs` co-resident
+// pairs.  Grouped (sched 1) when every split tile gets a group of at least
+// 2 pairs (or no tile is split): w = tiles / P whole tiles per pair, r =
+// tiles % P split tiles shared by g = min(8, P / r, K blocks) pairs each.
+// Otherwise stream-K (sched 0) over as many pairs as keep >= max(4, K
+// blocks / 4) units each, so a stream-K tile has at most 5 sharers.
+PairSchedule pair_schedule(long long tiles, int num_kb, int max_pairs, bool allow_grouped) {
+  PairSchedule s{};
+  max_pairs = std::max(1, max_pairs);
+  const long long w = tiles / max_pairs, r = tiles % max_pairs;
+  const long long g = r > 0 ? std::min<long long>(std::min<long long>(8, max_pairs / r), num_kb) : 0;
+  if (allow_grouped && (r == 0 || g >= 2)) {
+    s.sched = 1;
+    s.whole = (int)w;
+    s.split = (int)r;
+    s.group = (int)g;
+    s.pairs = w > 0 ? max_pairs : (int)(r * g);
+    return s;
+  }
+  const long long total = tiles * num_kb;
+  const long long min_units = std::max(4, (num_kb + 3) / 4);
+  s.sched = 0;
+  s.pairs = (int)std::max(1LL, std::min<long long>(max_pairs, total / min_units));
+  return s;
+}
+
+// Co-resident CTAs of the pair kernel with clusters of (2 x splits, 1, 1) and
+// the given dynamic shared memory (occupancy queries are slow: cached).
 long long pair_resident(int splits, int smem) {
   static long long cache[kMaxDevices][5][4] = {};
   static int cache_smem[kMaxDevices][5][4] = {};
@@ -326,14 +363,14 @@ long long pair_resident(int splits, int smem) {
   for (int i = 0; i < 4; ++i)
     if (cache_smem[dev][splits][i] == smem) return cache[dev][splits][i];
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2, 1, splits);
+  cfg.gridDim = dim3(2 * splits, 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.x = 2 * splits;
   attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = splits;
+  attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int clusters = 0;
@@ -359,8 +396,8 @@ size_t pair_workspace_bytes(int num_sms) { return 4096 + (size_t)num_sms * 256 *
 // CTA), BN = NP = the pair's weight rows per tile (<= 256; the gate_up
 // projection always 256 = 128 gate + the 128 matching up rows), n_tiles =
 // 2 x feature tiles, TMEM = two accumulators of pow2(NP) columns.
-// `splits` holds the number of pairs launched: as many as can be resident,
-// with at least max(4, K blocks / 4) units of work each.
+// `splits` holds the number of pairs launched (pair_schedule over the
+// co-resident pairs).
 GemmPlan plan_pair(DeviceState* ds, int T, int N, int K, bool silu_tiles, int* rc) {
   GemmPlan p{};
   p.BN = silu_tiles ? 256 : std::min(256, std::max(32, round_up(N, 32)));
@@ -376,19 +413,23 @@ GemmPlan plan_pair(DeviceState* ds, int T, int N, int K, bool silu_tiles, int* r
   p.tmem_cols = 2 * cols;
   *rc = ensure_smem(ds, 8u, gemm_pair_tcgen05_kernel, p.smem);
   if (*rc) return p;
-  const long long total = (long long)(p.n_tiles / 2) * p.token_tiles * p.num_kb;
-  long long pairs = pair_resident(1, p.smem) / 2;
-  pairs = std::min(pairs, (long long)ds->num_sms / 2);
-  // every pair takes at least a quarter of a tile's K blocks, so a tile is
-  // shared by at most 5 pairs (a finisher streams <= 4 partials)
-  const long long min_units = std::max(4, (p.num_kb + 3) / 4);
-  pairs = std::max(1LL, std::min(pairs, total / min_units));
+  const long long tiles = (long long)(p.n_tiles / 2) * p.token_tiles;
+  long long max_pairs = pair_resident(1, p.smem) / 2;
+  max_pairs = std::min(max_pairs, (long long)ds->num_sms / 2);
   const char* forced = getenv("B200_GEMM_PAIRS");
-  if (forced && *forced) pairs = std::max(1LL, std::min(pairs, (long long)atoi(forced)));
-  p.splits = (int)pairs;
+  if (forced && *forced) max_pairs = std::max(1LL, std::min(max_pairs, (long long)atoi(forced)));
+  const PairSchedule sc = pair_schedule(tiles, p.num_kb, (int)std::max(1LL, max_pairs), grouped_allowed());
+  p.sched = sc.sched;
+  p.grp_whole = sc.whole;
+  p.grp_split = sc.split;
+  p.grp_size = sc.group;
+  p.splits = sc.pairs;
   if (gemm_debug())
-    fprintf(stderr, "[b200 gemm pair] T=%d N=%d K=%d NP=%d tiles=%dx%d kb=%d pairs=%d stages=%d smem=%d\n",
-            T, N, K, p.BN, p.n_tiles / 2, p.token_tiles, p.num_kb, p.splits, p.stages, p.smem);
+    fprintf(stderr,
+            "[b200 gemm pair] T=%d N=%d K=%d NP=%d tiles=%dx%d kb=%d pairs=%d sched=%d whole=%d split=%d "
+            "group=%d stages=%d smem=%d\n",
+            T, N, K, p.BN, p.n_tiles / 2, p.token_tiles, p.num_kb, p.splits, p.sched, p.grp_whole,
+            p.grp_split, p.grp_size, p.stages, p.smem);
   return p;
 }
 
@@ -426,18 +467,25 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
   if (!silu && ldy < N) return fail(B200_ERR_INVALID, "linear: ldy < N");
   DeviceState* ds;
   if (int r = device_state(&ds)) return r;
-  // the SM-pair kernel when every pair gets at least one whole tile (large
-  // projections such as gate_up and the LM head: measured faster there);
-  // smaller problems would be mostly stream-K fix-ups, where the single-SM
-  // kernel's on-chip split-K is faster
+  // Kernel choice: the SM-pair kernel when every pair gets at least one
+  // whole tile (large projections such as gate_up and the LM head), where
+  // the grouped schedule's split-K exchange overlaps the MMAs of the whole
+  // tiles; otherwise the single-SM kernel with its on-chip cluster split-K
+  // (measured faster for the smaller projections: with no whole tile to hide
+  // it behind, the exchange through L2 costs more than it saves).
   const long long pair_tiles = (long long)(silu ? (N / 2 + 127) / 128 : (N + 255) / 256) *
                                ((T + 2 * kGemmBM - 1) / (2 * kGemmBM));
-  if (pair_enabled() && workspace != nullptr && aligned16(workspace) &&
-      ws_bytes >= pair_workspace_bytes(ds->num_sms) &&
-      (pair_tiles >= ds->num_sms / 2 || pair_forced())) {
+  const bool use_pair = pair_enabled() && workspace != nullptr && aligned16(workspace) &&
+                        ws_bytes >= pair_workspace_bytes(ds->num_sms) &&
+                        (pair_forced() || pair_tiles >= ds->num_sms / 2);
+  GemmPlan pp{};
+  if (use_pair) {
     int prc = 0;
-    const GemmPlan p = plan_pair(ds, T, N, K, silu, &prc);
+    pp = plan_pair(ds, T, N, K, silu, &prc);
     if (prc) return prc;
+  }
+  if (use_pair) {
+    const GemmPlan& p = pp;
     CUtensorMap tmW, tmX;
     if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK,
                           (uint32_t)(p.BN / 2)))
@@ -457,6 +505,10 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
     a.tiles_t = p.token_tiles;
     a.sk_flags = static_cast<unsigned*>(workspace);
     a.sk_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + 4096);
+    a.sched = p.sched;
+    a.grp_whole = p.grp_whole;
+    a.grp_split = p.grp_split;
+    a.grp_size = p.grp_size;
     a.err = ds->err;
     // outputs by TMA tensor stores: box of 32 features x 128 tokens, 64-byte
     // swizzle (the kernel's staging layout)
@@ -667,10 +719,48 @@ int b200_linear_workspace_bytes(int T, int N, int K, size_t* bytes) {
   if (!bytes || T < 0 || N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "bad arguments");
   DeviceState* ds;
   if (int r = device_state(&ds)) return r;
-  // the persistent SM-pair kernel's stream-K flags and partial tiles (the
+  // the persistent SM-pair kernel's split-K flags and partial tiles (the
   // same bound for every shape, so one buffer serves every GEMM)
   *bytes = pair_workspace_bytes(ds->num_sms);
   return B200_OK;
+}
+
+int b200_gemm_schedule_check(long long tiles, int num_kb, int max_pairs, int grouped) {
+  if (tiles <= 0 || tiles > (1LL << 22) || num_kb <= 0 || num_kb > 4096 || max_pairs <= 0 ||
+      max_pairs > 512 || tiles * num_kb > (1LL << 24))
+    return fail(B200_ERR_INVALID, "schedule check: bad arguments");
+  const PairSchedule sc = pair_schedule(tiles, num_kb, max_pairs, grouped != 0);
+  std::string cover((size_t)(tiles * num_kb), '\0');
+  long long bad = 0;
+  if (sc.pairs < 1 || sc.pairs > max_pairs) ++bad;
+  // flag area: 2 words per pair below the done counters, which fit the 4 KiB
+  if (2 * sc.pairs > kGrpDoneOffset || kGrpDoneOffset + 2 * sc.split > 1024) ++bad;
+  const long long total = tiles * num_kb;
+  for (int pr = 0; pr < sc.pairs && pr >= 0; ++pr) {
+    long long u = total * pr / sc.pairs;
+    const long long u_end = total * (pr + 1) / sc.pairs;
+    int k = 0;
+    PairSeg sg;
+    long long segs = 0;
+    while (pair_next_seg(sc.sched, tiles, num_kb, sc.whole, sc.split, sc.group, pr, sc.pairs, u, u_end, k, sg)) {
+      if (++segs > total + 1) return fail(B200_ERR_INVALID, "schedule check: pair %d does not terminate", pr);
+      if (sg.tile < 0 || sg.tile >= tiles || sg.kbb < 0 || sg.kbe > num_kb || sg.kbb >= sg.kbe) {
+        ++bad;
+        continue;
+      }
+      // a grouped member is pair tile * g + member of a split tile
+      if (sg.member >= 0 &&
+          (sc.sched != 1 || sg.tile >= sc.split || sg.tile * sc.group + sg.member != pr || sg.member >= sc.group))
+        ++bad;
+      for (int kb = sg.kbb; kb < sg.kbe; ++kb) {
+        char& c = cover[(size_t)(sg.tile * num_kb + kb)];
+        if (c < 2) ++c;
+      }
+    }
+  }
+  for (char c : cover)
+    if (c != 1) ++bad;
+  return (int)std::min<long long>(bad, 1 << 30);
 }
 
 int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,

@@ -156,6 +156,12 @@ __device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const CUtensorMap
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders this thread's view of global memory (e.g. data another SM published
+// and this thread acquired) before its subsequent async-proxy (TMA / bulk
+// copy) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
 // ---------------------------------------------------------------------------
 // thread-block clusters / distributed shared memory

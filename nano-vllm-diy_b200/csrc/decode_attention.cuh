@@ -18,10 +18,15 @@
 //           the ring keeps streaming across item boundaries and no CTA-wide
 //           barrier is taken in the main loop.
 //   merge = a sequence spanning several items writes per-item fp32 partials
-//           (m, l, o) with plain stores; after a grid-wide barrier (the
-//           launch is cooperative, so every CTA is resident) all warps take
-//           the split (sequence, kv head) pairs from a second queue and merge
-//           them.  A single-item sequence writes its output directly.
+//           (m, l, o) and bumps the completion counter of its (sequence, kv
+//           head) unit.  A warp whose item queue has run dry takes the split
+//           units, in sequence order, from a second queue, waits (bounded)
+//           for the unit's items and merges them in one online-softmax pass,
+//           so the merges overlap the other warps' last items instead of
+//           following a grid-wide barrier.  A single-item sequence writes its
+//           output directly.  (The launch is cooperative: every CTA is
+//           resident, and a unit's items are all taken by running warps
+//           before any warp waits on it.)
 // The launch shape depends only on the SM count; context lengths are read
 // from cu_seqlens_k on the device (CUDA-graph safe; rows with q length <= 0
 // are graph padding and are skipped).
@@ -42,10 +47,12 @@ constexpr int kDecMaxKvHeads = 64;
 constexpr int kDecStK = 0, kDecStV = 8192, kDecStQ = 16384;
 constexpr int kDecStageBytes = 18432;
 constexpr int kDecWarpBytes = kDecStages * kDecStageBytes;
-// workspace head: the scheduler words {next item, warps done, warps at the
-// grid barrier, next merge unit, warps merged}; zero between calls (the last
-// warp of each phase resets them)
-constexpr int kDecSchedBytes = 256;
+// workspace head: the scheduler words {next item, warps out of the item
+// queue, (unused), next merge unit, warps out of the merge queue} in the first
+// 256 bytes, then the per-(sequence, kv head) completion counters
+// [kDecMaxSeqs][kDecMaxKvHeads]; all zero between calls (the last warp out of
+// each queue resets its words, a merge zeroes its counter)
+constexpr int kDecSchedBytes = 256 + kDecMaxSeqs * kDecMaxKvHeads * 4;
 
 struct DecodeArgs {
   const int* block_tables;
@@ -55,7 +62,7 @@ struct DecodeArgs {
   int B, Hq, Hkv, G, page, q_box_rows;
   long long num_slots;
   float scale_log2;      // softmax_scale * log2(e)
-  int* sched;            // workspace head (kDecSchedBytes)
+  int* sched;            // workspace head (kDecSchedBytes): scheduler words, then unit counters
   float* part_ml;        // [cap_items][Hq][2]
   float* part_o;         // [cap_items][Hq][128]
   long long cap_items;
@@ -71,6 +78,13 @@ struct DecTile {
   long long row;  // cache row (slot) of the tile's first token
   int j0;         // iterator: the item's first token in the sequence
 };
+
+// Release-ordered increment: this thread's earlier writes, and those of the
+// lanes ordered before it by __syncwarp, are visible to whoever acquires the
+// new value (no separate fence instruction).
+__device__ __forceinline__ void red_release_gpu_add_s32(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
   int v;
@@ -104,6 +118,7 @@ __global__ void __launch_bounds__(128, 1)
                                        kDecWarps * kDecStages * sizeof(DecTile));
   int* s_start = s_scan + 8;
   int* sched = a.sched;
+  int* unit_done = a.sched + 64;  // [b * Hkv + h]: items of the unit published
 
   if (lane == 0) {
     for (int i = 0; i < kDecStages; ++i) mbar_init(&s_bar[i], 1);
@@ -261,6 +276,18 @@ __global__ void __launch_bounds__(128, 1)
   float ot[8][4];                            // O^T: 8 tiles of 16 dims
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // head columns 2tq, 2tq+1
   int consumed = 0;
+  // the unit whose partial this warp wrote last and has not yet published:
+  // its counter is bumped just before the warp's next item stores (or when
+  // the warp leaves the item loop), so the release finds those stores long
+  // completed instead of stalling on fresh ones
+  int pending_unit = -1;
+  auto publish_pending = [&]() {
+    if (pending_unit >= 0) {
+      __syncwarp();
+      if (lane == 0) red_release_gpu_add_s32(&unit_done[pending_unit], 1);
+      pending_unit = -1;
+    }
+  };
 
   for (int t = 0; t < valid_issued; ++t) {
     __syncwarp();
@@ -381,6 +408,7 @@ __global__ void __launch_bounds__(128, 1)
 
     if (!d.last) continue;
     // ---- item done: output (single item) or split-KV partial
+    publish_pending();
     if (d.npages == 1) {
       // O / l, transposed back to [head][dim] rows: 4-byte stores of dim pairs
       const float inv0 = l_run[0] > 0.f ? 1.f / l_run[0] : 0.f;
@@ -414,7 +442,9 @@ __global__ void __launch_bounds__(128, 1)
           *reinterpret_cast<float2*>(a.part_ml + ((size_t)d.c * a.Hq + hq) * 2) = make_float2(m_run[e], l_run[e]);
       }
     }
+    pending_unit = d.b * a.Hkv + d.h;
   }
+  publish_pending();
   // drain: every issued tile has landed before the CTA's shared memory is released
   if (lane == 0) {
     for (int t = consumed; t < valid_issued; ++t)
@@ -422,25 +452,10 @@ __global__ void __launch_bounds__(128, 1)
   }
   __syncwarp();
 
-  // ---- grid barrier: every warp's partials are written (the launch is
-  // cooperative, so all CTAs are resident; the wait is bounded)
-  if (lane == 0) {
-    __threadfence();
-    atomicAdd(&sched[2], 1);
-    const unsigned long long t0 = globaltimer_ns();
-    while (ld_acquire_gpu_s32(&sched[2]) < nwarps) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        raise_error(a.err, ERR_PEER_TIMEOUT);
-        break;
-      }
-    }
-  }
-  __syncwarp();
-
   // ---- merge phase: (sequence, kv head) units of sequences split into
-  // several items, taken from a queue by every warp.  Each lane owns 4 of the
-  // 128 dims of every head of the group; loads are batched over items and
-  // heads so a merge costs a few memory round trips.
+  // several items, from a second queue in sequence order.  Each lane owns 4
+  // of the 128 dims of every head of the group; one online-softmax pass over
+  // the items, loads batched over 2 items x every head.
   const int units = a.B * a.Hkv;
   while (true) {
     int u = 0;
@@ -450,6 +465,20 @@ __global__ void __launch_bounds__(128, 1)
     const int b = u / a.Hkv, h = u - b * a.Hkv;
     const int c0 = s_start[b], np = s_start[b + 1] - c0;
     if (np <= 1) continue;  // written directly (or an empty row)
+    if (lane == 0) {
+      // the unit's items were all taken before this queue opened: wait
+      // (bounded) until they are published, then zero the counter
+      const unsigned long long t0 = globaltimer_ns();
+      while (ld_acquire_gpu_s32(&unit_done[u]) < np) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          raise_error(a.err, ERR_PEER_TIMEOUT);
+          break;
+        }
+        __nanosleep(128);
+      }
+      unit_done[u] = 0;
+    }
+    __syncwarp();
     const int G = a.G;
     float M[8], L[8];
     float4 acc[8];
@@ -459,19 +488,6 @@ __global__ void __launch_bounds__(128, 1)
       L[gg] = 0.f;
       acc[gg] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    // pass 1: the maxima, lanes over items
-    for (int p0 = 0; p0 < np; p0 += 32) {
-      const int pp = p0 + lane;
-#pragma unroll
-      for (int gg = 0; gg < 8; ++gg)
-        if (gg < G && pp < np)
-          M[gg] = fmaxf(M[gg], __ldcg(a.part_ml + ((size_t)(c0 + pp) * a.Hq + (size_t)h * G + gg) * 2));
-    }
-#pragma unroll
-    for (int gg = 0; gg < 8; ++gg)
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) M[gg] = fmaxf(M[gg], __shfl_xor_sync(0xffffffffu, M[gg], off));
-    // pass 2: weighted sums, 2 items x every head per batch of loads
     for (int p0 = 0; p0 < np; p0 += 2) {
       float2 ml[2][8];
       float4 ov[2][8];
@@ -490,10 +506,17 @@ __global__ void __launch_bounds__(128, 1)
       for (int uu = 0; uu < 2; ++uu)
 #pragma unroll
         for (int gg = 0; gg < 8; ++gg) {
-          const float w = ml[uu][gg].x == -INFINITY ? 0.f : fast_exp2(ml[uu][gg].x - M[gg]);
-          L[gg] += w * ml[uu][gg].y;
-          acc[gg].x += w * ov[uu][gg].x; acc[gg].y += w * ov[uu][gg].y;
-          acc[gg].z += w * ov[uu][gg].z; acc[gg].w += w * ov[uu][gg].w;
+          const float mi = ml[uu][gg].x;
+          if (mi == -INFINITY) continue;  // padding or an empty item
+          const float mn = fmaxf(M[gg], mi);
+          const float sc = fast_exp2(M[gg] - mn);  // 0 while M is -inf
+          const float w = fast_exp2(mi - mn);
+          L[gg] = L[gg] * sc + w * ml[uu][gg].y;
+          acc[gg].x = acc[gg].x * sc + w * ov[uu][gg].x;
+          acc[gg].y = acc[gg].y * sc + w * ov[uu][gg].y;
+          acc[gg].z = acc[gg].z * sc + w * ov[uu][gg].z;
+          acc[gg].w = acc[gg].w * sc + w * ov[uu][gg].w;
+          M[gg] = mn;
         }
     }
     const int qrow = a.cu_q[b];
@@ -508,9 +531,8 @@ __global__ void __launch_bounds__(128, 1)
           packed;
     }
   }
-  // the last warp out resets the merge queue and the barrier for the next call
+  // the last warp out of the merge queue resets it for the next call
   if (lane == 0 && atomicAdd(&sched[4], 1) == nwarps - 1) {
-    atomicExch(&sched[2], 0);
     atomicExch(&sched[3], 0);
     atomicExch(&sched[4], 0);
   }

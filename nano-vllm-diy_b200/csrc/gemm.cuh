@@ -83,6 +83,13 @@ struct GemmArgs {
   unsigned* sk_flags;  // [pairs * 2] partial-ready flags (zero between launches)
   float* sk_part;      // [pairs * 2][BN][128] fp32 partial tiles
   int use_tma_store;   // outputs written by TMA tensor stores (needs y 16-byte aligned, ldy % 8 == 0)
+  // schedule of the SM-pair kernel: 0 stream-K over the flat (tile, K block)
+  // units; 1 grouped: split tiles [0, grp_split) are shared by grp_size pairs
+  // each (pair p < grp_split * grp_size takes K share p % grp_size of tile
+  // p / grp_size first), then every pair takes grp_whole whole tiles
+  // grp_split + p + j * pairs
+  int sched;
+  int grp_whole, grp_split, grp_size;
   unsigned* err;
   AllReducePeers ar;   // EPI_ALLREDUCE only
 };
@@ -121,15 +128,32 @@ __device__ __forceinline__ bool wait_flag_and_reset(unsigned* p, unsigned want, 
   return true;
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  // Eager semantics of src/layers/activation.py:9-10 on bf16 tensors: silu
-  // is rounded to bf16, then the product is rounded again.  The sigmoid uses
-  // the hardware exp2 / reciprocal paths (__expf, __fdividef): their last-bit
-  // fp32 differences from expf and IEEE division disappear in the bf16
-  // rounding except for rare one-ulp cases, and they are several times
-  // cheaper, which matters in a GEMM epilogue.
-  const float s = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
-  return bf16_round(__fmul_rn(s, u));
+// bf16 rounding (to nearest even) of two floats by one packed conversion,
+// unpacked with integer shifts: half the conversions of two bf16_round calls
+// (conversions issue at a fraction of the FP32 rate and bound the SiLU
+// epilogue otherwise).
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t w = pack_bf16x2(a, b);
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xFFFF0000u);
+}
+
+// Eager semantics of src/layers/activation.py:9-10 on bf16 tensors, for two
+// lanes: g and u are the GEMM outputs rounded to bf16, silu(g) is rounded to
+// bf16, then multiplied by u.  The product is returned in g0 / g1 UNROUNDED:
+// every caller stores it through a round-to-nearest bf16 conversion, which is
+// the eager op's final rounding.  The sigmoid uses the hardware exp2 /
+// reciprocal paths (__expf, __fdividef): their last-bit fp32 differences from
+// expf and IEEE division disappear in the bf16 rounding except for rare
+// one-ulp cases, and they are several times cheaper.
+__device__ __forceinline__ void silu_mul2(float& g0, float& g1, float u0, float u1) {
+  bf16_round2(g0, g1);
+  bf16_round2(u0, u1);
+  float s0 = __fdividef(g0, 1.0f + __expf(-g0));
+  float s1 = __fdividef(g1, 1.0f + __expf(-g1));
+  bf16_round2(s0, s1);
+  g0 = __fmul_rn(s0, u0);
+  g1 = __fmul_rn(s1, u1);
 }
 
 // Epilogue shared by the GEMM kernels: this CTA's token rows [tb, te) of
@@ -152,7 +176,11 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, SumFn& sum8, in
       sum8(t * kGemmBM + ch * 8, g);
       sum8(t * kGemmBM + 64 + ch * 8, up);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = silu_mul(bf16_round(g[i]), bf16_round(up[i]));
+      for (int i = 0; i < 8; i += 2) {
+        o[i] = g[i];
+        o[i + 1] = g[i + 1];
+        silu_mul2(o[i], o[i + 1], up[i], up[i + 1]);
+      }
       __nv_bfloat16* dst = p.y + (size_t)(t0 + t) * p.ldy + feat;
       if (p.vec_ok && feat + 8 <= p.silu_inter) {
         uint4 pk;

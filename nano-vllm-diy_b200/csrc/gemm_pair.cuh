@@ -164,7 +164,72 @@ __device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs
 // last, so a finisher never waits on work queued behind a wait.
 // TMEM holds two accumulators (2 x NP columns): the MMA issuer fills one
 // while the epilogue warps drain the other.
+//
+// Grouped schedule (p.sched = 1; the default whenever it balances): with P
+// pairs and n tiles, w = n / P whole tiles per pair and r = n % P split
+// tiles, each shared by a group of g = min(8, P / r, K blocks) pairs.  Pair
+// p < r g first computes K share p % g of split tile p / g, then whole tiles
+// r + p + j P (j < w).  Every member of a group owns the 32-wide output
+// chunks m, m + g, ... (SiLU: gate / up chunk pairs): it writes the chunks
+// the other members own to its partial slot, raises its flag, waits for the
+// flags of the members whose chunks it owns (all pairs are co-resident and
+// the members start together), then sums its own chunks from TMEM and the
+// members' partials and writes them.  The reduction is spread over all
+// members, and for w >= 1 it overlaps the MMAs of the next whole tile.  The
+// last member to finish resets the group's flags for the next launch.
 // ---------------------------------------------------------------------------
+
+// One segment of a pair's work: K blocks [kbb, kbe) of `tile`; `member` is
+// the pair's index in the tile's group under the grouped schedule (-1 for
+// whole tiles and stream-K segments).
+struct PairSeg {
+  long long tile;
+  int kbb, kbe, member;
+};
+
+// The segments of pair `pr` of `pairs` in order, walked identically by the
+// producer, the MMA issuer and the epilogue (and by the host-side coverage
+// check).  State: `u` (stream-K: next unit, starts at the pair's first unit)
+// and `k` (grouped: segments taken, starts at 0).
+__host__ __device__ inline bool pair_next_seg(int sched, long long tiles, int num_kb, int grp_whole,
+                                              int grp_split, int grp_size, int pr, int pairs,
+                                              long long& u, long long u_end, int& k, PairSeg& s) {
+  if (sched == 0) {
+    if (u >= u_end) return false;
+    s.tile = u / num_kb;
+    s.kbb = (int)(u - s.tile * num_kb);
+    const long long left = u_end - u;
+    s.kbe = left < (long long)(num_kb - s.kbb) ? s.kbb + (int)left : num_kb;
+    s.member = -1;
+    u += s.kbe - s.kbb;
+    return true;
+  }
+  int j = k;
+  if (grp_size > 0 && pr < grp_split * grp_size) {
+    if (j == 0) {
+      const int m = pr % grp_size;
+      s.tile = pr / grp_size;
+      s.kbb = (int)((long long)m * num_kb / grp_size);
+      s.kbe = (int)((long long)(m + 1) * num_kb / grp_size);
+      s.member = m;
+      ++k;
+      return true;
+    }
+    --j;
+  }
+  if (j >= grp_whole) return false;
+  s.tile = grp_split + pr + (long long)j * pairs;
+  if (s.tile >= tiles) return false;
+  s.kbb = 0;
+  s.kbe = num_kb;
+  s.member = -1;
+  ++k;
+  return true;
+}
+
+// Word offset of the grouped schedule's per-(split tile, CTA half) done
+// counters in the flag area (the partial-ready flags use words [0, 2 pairs)).
+constexpr int kGrpDoneOffset = 512;
 
 // Partial tiles are [NP/32 chunks] of 16 KiB, each [8][128 tokens][4
 // features] fp32: a thread's 32 columns of a chunk are 8 float4 at stride
@@ -205,9 +270,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t leader = crank & ~1u;
   const int pr = blockIdx.x >> 1;
   const int pairs = gridDim.x >> 1;
-  const long long total = (long long)p.tiles_m * p.tiles_t * p.num_kb;
+  const long long tiles = (long long)p.tiles_m * p.tiles_t;
+  const long long total = tiles * p.num_kb;
+  // stream-K: this pair's units (unused by the grouped schedule)
   const long long u_begin = sk_begin(total, pr, pairs);
   const long long u_end = sk_begin(total, pr + 1, pairs);
+  auto next_seg = [&](long long& u, int& k, PairSeg& sg) {
+    return pair_next_seg(p.sched, tiles, p.num_kb, p.grp_whole, p.grp_split, p.grp_size, pr, pairs, u,
+                         u_end, k, sg);
+  };
   const uint32_t acc_stride = (uint32_t)p.tmem_cols / 2;  // columns per accumulator
   // output features of a tile: NP (plain) or the 128 gate rows (SiLU)
   const int tile_feats = silu ? 128 : NP;
@@ -248,12 +319,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t full_leader = map_to_rank(smem_u32(full), leader);
       int it = 0;
       bool ok = true;
-      for (long long u = u_begin; u < u_end && ok;) {
-        const long long tile = u / p.num_kb;
-        const int kbb = (int)(u - tile * p.num_kb);
-        const int kbe = (int)min((long long)p.num_kb, kbb + (u_end - u));
-        const int mt = (int)(tile / p.tiles_t);
-        const int tt = (int)(tile - (long long)mt * p.tiles_t);
+      long long su = u_begin;
+      int sk = 0;
+      PairSeg sg;
+      while (ok && next_seg(su, sk, sg)) {
+        const int kbb = sg.kbb, kbe = sg.kbe;
+        const int mt = (int)(sg.tile / p.tiles_t);
+        const int tt = (int)(sg.tile - (long long)mt * p.tiles_t);
         const int tok = tt * 2 * kGemmBM + (int)v * kGemmBM;
         // weight rows: plain = features mt*NP + v*NP/2; SiLU = gate rows
         // (leader) or the matching up rows (peer) of features mt*128
@@ -271,7 +343,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tma_load_2d_pair(smem_u32(a_smem + (size_t)s * kABytes), &tmX, bar, kc, tok);
           tma_load_2d_pair(smem_u32(b_smem + (size_t)s * b_bytes), &tmW, bar, kc, wrow);
         }
-        u += kbe - kbb;
       }
       if (!ok && v == 0) {
         // drain the copies still in flight before the CTA can exit
@@ -289,10 +360,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t accf_peer = map_to_rank(smem_u32(acc_full), leader + 1u);
       int it = 0, seg = 0;
       bool ok = true;
-      for (long long u = u_begin; u < u_end && ok; ++seg) {
-        const long long tile = u / p.num_kb;
-        const int kbb = (int)(u - tile * p.num_kb);
-        const int kbe = (int)min((long long)p.num_kb, kbb + (u_end - u));
+      long long su = u_begin;
+      int sk = 0;
+      PairSeg sg;
+      for (; ok && next_seg(su, sk, sg); ++seg) {
+        const int kbb = sg.kbb, kbe = sg.kbe;
         const int b = seg & 1;
         // the epilogues of both CTAs have drained this accumulator
         if (!mbar_wait(&acc_empty[b], (((uint32_t)seg >> 1) & 1u) ^ 1u, p.err)) break;
@@ -318,7 +390,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_commit_pair(accf_own + (uint32_t)b * 8u);
         tc_commit_pair(accf_peer + (uint32_t)b * 8u);
-        u += kbe - kbb;
       }
     }
   } else {
@@ -332,19 +403,238 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     auto chunk_at = [&](int i) { return silu ? ((i & 1) ? nchunks / 2 + (i >> 1) : (i >> 1)) : i; };
     bool ok = true;
     int seg = 0;
-    for (long long u = u_begin; u < u_end; ++seg) {
-      const long long tile = u / p.num_kb;
-      const int kbb = (int)(u - tile * p.num_kb);
-      const int kbe = (int)min((long long)p.num_kb, kbb + (u_end - u));
+    // output chunks staged so far (staging buffer = outs & 3); it keeps
+    // counting across segments, so the buffer written next was last used four
+    // stores ago, which the wait after every store has retired
+    int outs = 0;
+    // one output chunk: bias / SiLU already applied, bf16 rounding here;
+    // staged for a TMA store (64-byte swizzle) or stored from registers
+    auto emit_chunk = [&](float (&a)[32], int f0, int fmax, int row0, int tok) {
+      if (p.use_tma_store) {
+        const bool staged = f0 < fmax && row0 < p.T;  // uniform over the CTA
+        uint8_t* stg = stage_out + (outs & 3) * (kGemmBM * 64);
+        if (staged) {
+          const uint32_t sw = (uint32_t)((row >> 1) & 3);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(stg + row * 64 + ((j ^ sw) * 16)) =
+                make_uint4(pack_bf16x2(a[8 * j], a[8 * j + 1]), pack_bf16x2(a[8 * j + 2], a[8 * j + 3]),
+                           pack_bf16x2(a[8 * j + 4], a[8 * j + 5]), pack_bf16x2(a[8 * j + 6], a[8 * j + 7]));
+          fence_proxy_async_smem();
+        }
+        epi_bar_sync();
+        if (staged) {
+          if (lead_thread) {
+            tma_store_2d(&tmY, smem_u32(stg), f0, row0);
+            bulk_commit_group();
+            bulk_wait_group_read<2>();  // the buffer written two stores from now is free
+          }
+          ++outs;
+        }
+      } else if (tok < p.T && f0 < fmax) {
+        __nv_bfloat16* dst = p.y + (size_t)tok * p.ldy + f0;
+        if (p.vec_ok && f0 + 32 <= fmax) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            reinterpret_cast<uint4*>(dst)[j] =
+                make_uint4(pack_bf16x2(a[8 * j], a[8 * j + 1]), pack_bf16x2(a[8 * j + 2], a[8 * j + 3]),
+                           pack_bf16x2(a[8 * j + 4], a[8 * j + 5]), pack_bf16x2(a[8 * j + 6], a[8 * j + 7]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (f0 + j < fmax) dst[j] = __float2bfloat16_rn(a[j]);
+        }
+      }
+    };
+    long long su = u_begin;
+    int sk = 0;
+    PairSeg sg;
+    for (; next_seg(su, sk, sg); ++seg) {
+      const long long tile = sg.tile;
+      const int kbb = sg.kbb, kbe = sg.kbe;
       const int mt = (int)(tile / p.tiles_t);
       const int tt = (int)(tile - (long long)mt * p.tiles_t);
       const int tok = tt * 2 * kGemmBM + (int)v * kGemmBM + row;  // this thread's token
       const int f_base = mt * tile_feats;
-      const bool contributor = kbb > 0;
-      const bool finisher = kbb == 0 && kbe < p.num_kb;
+      const bool contributor = sg.member < 0 && kbb > 0;
+      const bool finisher = sg.member < 0 && kbb == 0 && kbe < p.num_kb;
       const int b = seg & 1;
       if (ok) ok = mbar_wait(&acc_full[b], ((uint32_t)seg >> 1) & 1u, p.err);
       tc_fence_after();
+      if (sg.member >= 0) {
+        // ---- grouped split-K member (see the schedule notes above)
+        const int g = p.grp_size, me = sg.member;
+        const int first = (int)tile * g;  // the group's pairs: first .. first + g - 1
+        const int nout = silu ? nchunks / 2 : nchunks;
+        const int hn = silu ? nchunks / 2 : 0;  // SiLU: up chunk of output o is o + hn
+        const uint32_t d = tmem_base + (uint32_t)b * acc_stride + ((uint32_t)(q * 32) << 16);
+        float* my_part = p.sk_part + ((size_t)pr * 2 + v) * (size_t)NP * kGemmBM;
+        // pass 1: the chunks of outputs other members own -> this CTA's
+        // partial slot; the TMEM load of the next such chunk overlaps the
+        // stores of this one
+        auto owned = [&](int ch) { return ((silu ? ch % hn : ch) % g) == me; };
+        auto next_pub = [&](int ch) {
+          do {
+            ++ch;
+          } while (ch < nchunks && owned(ch));
+          return ch;
+        };
+        {
+          uint32_t rc[32], rn[32];
+          int ch = next_pub(-1);
+          if (ch < nchunks) {
+            tmem_ld_32x32b_x32(d + (uint32_t)(ch * 32), rc);
+            tmem_ld_wait_regs(rc);
+          }
+          while (ch < nchunks) {
+            const int nx = next_pub(ch);
+            if (nx < nchunks) tmem_ld_32x32b_x32(d + (uint32_t)(nx * 32), rn);
+            float4* dst = reinterpret_cast<float4*>(my_part + (size_t)ch * kChunkFloats) + row;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(dst + j * kGemmBM, make_float4(__uint_as_float(rc[4 * j]), __uint_as_float(rc[4 * j + 1]),
+                                                    __uint_as_float(rc[4 * j + 2]), __uint_as_float(rc[4 * j + 3])));
+            if (nx < nchunks) tmem_ld_wait_regs(rn);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) rc[j] = rn[j];
+            ch = nx;
+          }
+        }
+        __threadfence();
+        epi_bar_sync();
+        if (lead_thread) st_release_gpu(p.sk_flags + (size_t)pr * 2 + v, 1u);
+        if (me < nout) {
+          // pass 2: wait for the other members' partials (bounded), then sum
+          // this member's outputs: own TMEM first, the members in order after
+          __shared__ int s_grp_ok;
+          if (lead_thread) {
+            bool all = true;
+            for (int m = 0; m < g && all; ++m) {
+              if (m == me) continue;
+              unsigned* f = p.sk_flags + (size_t)(first + m) * 2 + v;
+              const unsigned long long t_start = globaltimer_ns();
+              while (ld_acquire_gpu(f) == 0u) {
+                if (globaltimer_ns() - t_start > kWaitLimitNs) {
+                  raise_error(p.err, ERR_PEER_TIMEOUT);
+                  all = false;
+                  break;
+                }
+              }
+            }
+            s_grp_ok = all;
+          }
+          // With no whole tile after this segment the stage ring is idle
+          // (every MMA of the pair has completed): the members' chunks this
+          // CTA needs are pulled into it by one burst of bulk copies (slot
+          // (owned output, member, gate/up)); otherwise they are read with
+          // plain loads, two members per round trip.
+          const int H = silu ? 2 : 1;
+          const int n_own = (nout - me + g - 1) / g;
+          const int copies = n_own * (g - 1) * H;
+          const int ring_slots = (int)(((size_t)S * (kABytes + b_bytes)) / (kChunkFloats * 4));
+          const bool burst = p.grp_whole == 0 && copies <= ring_slots && copies <= 32;
+          if (burst && lead_thread && s_grp_ok) {
+            fence_proxy_async_global();  // the acquired partials, then bulk reads of them
+            mbar_arrive_expect_tx(&fix_bar[0], (uint32_t)copies * kChunkFloats * 4);
+            int k = 0;
+            for (int o = me; o < nout; o += g)
+              for (int m = 0; m < g; ++m) {
+                if (m == me) continue;
+                for (int h = 0; h < H; ++h, ++k)
+                  bulk_load(smem_u32(smem) + (uint32_t)k * kChunkFloats * 4,
+                            p.sk_part + ((size_t)(first + m) * 2 + v) * (size_t)NP * kGemmBM +
+                                (size_t)(o + h * hn) * kChunkFloats,
+                            kChunkFloats * 4, &fix_bar[0]);
+              }
+          }
+          epi_bar_sync();
+          const bool peers_ok = s_grp_ok != 0;
+          const bool burst_ok = burst && peers_ok && mbar_wait(&fix_bar[0], 0u, p.err);
+          int oi = 0;  // owned-output index (burst slots)
+          auto group_chunk = [&](int ch, float (&a)[32]) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(d + (uint32_t)(ch * 32), r);
+            tmem_ld_wait_regs(r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = ok ? __uint_as_float(r[j]) : 0.f;
+            if (!peers_ok) return;
+            if (burst) {
+              if (!burst_ok) return;
+              const int h = (silu && ch >= hn) ? 1 : 0;
+              int mi = 0;
+              for (int m = 0; m < g; ++m) {
+                if (m == me) continue;
+                const float4* src = reinterpret_cast<const float4*>(
+                                        smem + (size_t)((oi * (g - 1) + mi) * H + h) * kChunkFloats * 4) + row;
+                float4 f[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[j] = src[j * kGemmBM];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  a[4 * j] += f[j].x; a[4 * j + 1] += f[j].y; a[4 * j + 2] += f[j].z; a[4 * j + 3] += f[j].w;
+                }
+                ++mi;
+              }
+              return;
+            }
+            auto part = [&](int m) {
+              return reinterpret_cast<const float4*>(p.sk_part +
+                                                     ((size_t)(first + m) * 2 + v) * (size_t)NP * kGemmBM +
+                                                     (size_t)ch * kChunkFloats) + row;
+            };
+            // the other members in order
+            for (int m = 0; m < g; ++m) {
+              if (m == me) continue;
+              const float4* src = part(m);
+              float4 f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __ldcg(src + j * kGemmBM);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                a[4 * j] += f[j].x; a[4 * j + 1] += f[j].y; a[4 * j + 2] += f[j].z; a[4 * j + 3] += f[j].w;
+              }
+            }
+          };
+          const int row0 = tt * 2 * kGemmBM + (int)v * kGemmBM;
+          for (int o = me; o < nout; o += g) {
+            float acc[32];
+            group_chunk(o, acc);
+            int f0, fmax;
+            if (silu) {
+              float up[32];
+              group_chunk(o + hn, up);
+#pragma unroll
+              for (int j = 0; j < 32; j += 2) silu_mul2(acc[j], acc[j + 1], up[j], up[j + 1]);
+              f0 = f_base + o * 32;
+              fmax = p.silu_inter;
+            } else {
+              f0 = f_base + o * 32;
+              fmax = p.N;
+              if (p.bias != nullptr) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (f0 + j < fmax) acc[j] += __bfloat162float(p.bias[f0 + j]);
+              }
+            }
+            emit_chunk(acc, f0, fmax, row0, tok);
+            ++oi;
+          }
+        }
+        // every TMEM load of this accumulator is done: release it; the last
+        // member of the group (this CTA half) resets the group's flags
+        tc_fence_before();
+        epi_bar_sync();
+        if (lead_thread) {
+          if (v == 0) mbar_arrive(&acc_empty[b]);
+          else mbar_arrive_cluster(acc_empty_leader + (uint32_t)b * 8u);
+          unsigned* done = p.sk_flags + kGrpDoneOffset + (size_t)tile * 2 + v;
+          if (atomicAdd(done, 1u) == (unsigned)(g - 1)) {
+            for (int m = 0; m < g; ++m) p.sk_flags[(size_t)(first + m) * 2 + v] = 0u;
+            *done = 0u;
+          }
+        }
+        continue;
+      }
       // contributors of this tile: pairs pr+1, ... whose ranges start inside it
       const long long tile_end = (tile + 1) * p.num_kb;
       int last_contrib = pr;
@@ -386,11 +676,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                   &fix_bar[slot]);
       };
       if (copies > 0 && lead_thread) {
+        fence_proxy_async_global();  // the acquired partials, then bulk reads of them
         fence_proxy_async_smem();
         for (int k = 0; k < min(copies, ring_slots); ++k) issue_copy(k);
       }
       float keep[32];  // SiLU: the gate chunk, held until its up chunk arrives
-      int outs = 0;    // output chunks staged in this segment (staging buffer = outs & 3)
       // the barrier after which every TMEM load of this accumulator is done
       const int rel_i = nchunks >= 2 ? nchunks - 2 : 0;
       uint32_t rc[32], rn[32];
@@ -433,7 +723,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               out = false;
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) acc[j] = silu_mul(bf16_round(keep[j]), bf16_round(acc[j]));
+              for (int j = 0; j < 32; j += 2) {
+                float g0 = keep[j], g1 = keep[j + 1];
+                silu_mul2(g0, g1, acc[j], acc[j + 1]);
+                acc[j] = g0;
+                acc[j + 1] = g1;
+              }
             }
             f0 = f_base + (ch - nchunks / 2) * 32;
             fmax = p.silu_inter;
@@ -518,7 +813,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lead_thread)
           for (int cq = pr + 1; cq <= last_contrib; ++cq) p.sk_flags[(size_t)cq * 2 + v] = 0u;
       }
-      u += kbe - kbb;
     }
     if (lead_thread && p.use_tma_store) bulk_wait_group_all();  // outputs written before exit
   }

@@ -37,6 +37,7 @@ _SIGNATURES = {
     "b200_launch_count": ([], ctypes.c_ulonglong),
     "b200_device_error": ([ctypes.POINTER(ctypes.c_uint), _i], _i),
     "b200_linear_workspace_bytes": ([_i, _i, _i, ctypes.POINTER(_sz)], _i),
+    "b200_gemm_schedule_check": ([ctypes.c_longlong, _i, _i, _i], _i),
     "b200_linear": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _c_void_p, _ll, _i, _i, _i,
                      _c_void_p, _sz, _c_void_p], _i),
     "b200_linear_silu_and_mul": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _ll, _i, _i, _i,

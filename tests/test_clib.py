@@ -48,3 +48,23 @@ def test_invalid_arguments_fail_before_any_launch():
     rc = lib.b200_rms_norm(ctypes.c_void_p(16), 12, None, ctypes.c_void_p(16), ctypes.c_void_p(16),
                            12, None, 1, 12, 1e-6, None)
     assert rc == -2
+
+
+def test_gemm_schedule_partitions_the_work():
+    """The SM-pair GEMM's work split (grouped split-K and stream-K), walked on
+    the host with the kernel's own segment iterator: every (tile, K block)
+    unit exactly once, groups of consecutive pairs, flags inside the flag
+    area.  Covers the Qwen3-8B decode shapes at every TP (tiles 3..594, 64 or
+    192 K blocks over 74 pairs) and forced pair counts."""
+    from src import b200
+    lib = b200.load_library()
+    cases = 0
+    for tiles in (1, 2, 3, 6, 12, 16, 23, 24, 37, 38, 48, 73, 74, 75, 96, 149, 297, 594):
+        for num_kb in (1, 2, 3, 7, 16, 64, 192):
+            for max_pairs in (1, 3, 17, 64, 74):
+                for grouped in (0, 1):
+                    bad = lib.b200_gemm_schedule_check(tiles, num_kb, max_pairs, grouped)
+                    assert bad == 0, (tiles, num_kb, max_pairs, grouped, bad)
+                    cases += 1
+    assert cases > 1000
+    assert lib.b200_gemm_schedule_check(0, 64, 74, 1) < 0

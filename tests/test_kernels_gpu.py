@@ -50,17 +50,20 @@ def test_linear(T, N, K):
     assert err <= 1e-2, err
 
 
-@pytest.mark.parametrize("kernel,pairs", [("pair", ""), ("pair", "1"), ("pair", "3"), ("pair", "17"),
-                                          ("single", "")])
+@pytest.mark.parametrize("kernel,pairs", [("grouped", ""), ("grouped", "1"), ("grouped", "3"),
+                                          ("grouped", "17"), ("streamk", ""), ("streamk", "3"),
+                                          ("streamk", "17"), ("single", "")])
 @pytest.mark.parametrize("T,N,K", [(256, 4096, 4096), (77, 1280, 2048), (513, 768, 1024),
-                                   (256, 24576, 1024)])
+                                   (256, 24576, 1024), (256, 6144, 4096)])
 def test_linear_kernels_and_splits(T, N, K, kernel, pairs, monkeypatch):
-    """Both GEMM kernels (persistent SM-pair tcgen05.mma.cta_group::2 with a
-    stream-K schedule, and single-SM) give the same product within
-    tolerance, whatever number of pairs shares the work (whole tiles,
-    contributor / finisher segments)."""
+    """Every GEMM schedule gives the same product within tolerance: the
+    SM-pair kernel (tcgen05.mma.cta_group::2) with its grouped split-K
+    schedule (whole tiles only, split tiles only, both) and with its
+    stream-K schedule (whole tiles, contributor / finisher segments),
+    whatever number of pairs shares the work, and the single-SM kernel."""
     from src import b200
-    monkeypatch.setenv("B200_GEMM_PAIR", "2" if kernel == "pair" else "0")
+    monkeypatch.setenv("B200_GEMM_PAIR", "0" if kernel == "single" else "2")
+    monkeypatch.setenv("B200_GEMM_SCHED", "streamk" if kernel == "streamk" else "")
     monkeypatch.setenv("B200_GEMM_PAIRS", pairs)
     x = randn(T, K, seed=11)
     w = randn(N, K, std=0.02, seed=12)
@@ -73,18 +76,26 @@ def test_linear_kernels_and_splits(T, N, K, kernel, pairs, monkeypatch):
     assert b200.device_error(clear=True) == 0
 
 
-def test_linear_bias_and_strided_out():
+@pytest.mark.parametrize("kernel,T", [("default", 48), ("grouped", 200), ("streamk", 200)])
+@pytest.mark.parametrize("col0", [0, 1])
+def test_linear_bias_and_strided_out(kernel, T, col0, monkeypatch):
+    """Bias and an output view with a row stride wider than N; col0 = 1 makes
+    the rows 2-byte aligned only, so the kernels store without TMA."""
     from src import b200
-    T, N, K = 48, 640, 1024
+    monkeypatch.setenv("B200_GEMM_PAIR", "1" if kernel == "default" else "2")
+    monkeypatch.setenv("B200_GEMM_SCHED", "streamk" if kernel == "streamk" else "")
+    N, K = 640, 1024
     x = randn(T, K, seed=3)
     w = randn(N, K, std=0.02, seed=4)
     b = randn(N, std=0.5, seed=5)
     ref = x.float() @ w.float().t() + b.float()
     out = torch.zeros(T, N + 64, dtype=torch.bfloat16, device=DEV)
-    b200.linear(x.to(DEV), w.to(DEV), b.to(DEV), out=out[:, :N])
+    b200.linear(x.to(DEV), w.to(DEV), b.to(DEV), out=out[:, col0:col0 + N])
     torch.cuda.synchronize()
-    assert L.rel_err(out[:, :N].cpu(), ref) <= 1e-2
-    assert torch.count_nonzero(out[:, N:]) == 0
+    assert L.rel_err(out[:, col0:col0 + N].cpu(), ref) <= 1e-2
+    assert torch.count_nonzero(out[:, :col0]) == 0
+    assert torch.count_nonzero(out[:, col0 + N:]) == 0
+    assert b200.device_error(clear=True) == 0
 
 
 @pytest.mark.parametrize("T,I,K", [(1, 64, 256), (40, 1536, 1024), (256, 3072, 1024), (256, 1536, 4096), (300, 512, 2048), (16, 96, 512)])
