@@ -312,10 +312,36 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* __res
   const __nv_bfloat16* lp = logits + (size_t)row * stride;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = __bfloat162float(lp[i]);
+  auto take = [&](float v, int i) {
     if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  };
+  int scalar_from = 0;
+  if ((reinterpret_cast<uintptr_t>(lp) & 15) == 0) {
+    // 16-byte loads (8 logits), four in flight per thread
+    const int nv = V >> 3;
+    const uint4* vp = reinterpret_cast<const uint4*>(lp);
+    for (int j = threadIdx.x; j < nv; j += 4 * blockDim.x) {
+      uint4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int jj = j + u * (int)blockDim.x;
+        q[u] = jj < nv ? __ldg(vp + jj) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int jj = j + u * (int)blockDim.x;
+        if (jj >= nv) continue;
+        const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          take(__uint_as_float(w[k] << 16), jj * 8 + 2 * k);
+          take(__uint_as_float(w[k] & 0xffff0000u), jj * 8 + 2 * k + 1);
+        }
+      }
+    }
+    scalar_from = nv << 3;
   }
+  for (int i = scalar_from + (int)threadIdx.x; i < V; i += blockDim.x) take(__bfloat162float(lp[i]), i);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);

@@ -254,6 +254,21 @@ def test_argmax_exact():
     assert y[3].item() == 100
 
 
+@pytest.mark.parametrize("rows,V,pad", [(5, 1001, 0), (3, 37, 0), (4, 4100, 4), (2, 16, 0)])
+def test_argmax_ragged_rows(rows, V, pad):
+    """Rows whose start is not 16-byte aligned (scalar loads), lengths that
+    are not a multiple of 8 (scalar tail after the 16-byte loads), ties."""
+    from src import b200
+    x = randn(rows, V + pad, seed=27)
+    x[0, V - 1] = 40.0  # maximum in the tail
+    x[rows - 1, 1] = 40.0
+    x[rows - 1, V - 2] = 40.0  # tie -> first index
+    xd = x.to(DEV)[:, :V]
+    y = b200.argmax(xd)
+    torch.cuda.synchronize()
+    assert torch.equal(y.cpu(), torch.argmax(x[:, :V], -1))
+
+
 # --------------------------------------------------------------------------- attention
 def _paged_case(lens_q, lens_k, Hq, Hkv, page=256, seed=30, extra_blocks=3):
     g = _g(seed)
