@@ -406,22 +406,21 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // everything above overlaps the previous kernel's tail (programmatic
-  // dependent launch); activations and peer buffers are read below
-  griddep_wait();
-  griddep_launch_dependents();
+  // dependent launch), and so do the producer's weight loads for the first
+  // ring stages (weights are parameters; no kernel of the step writes them);
+  // activations, outputs and peer buffers are touched only after the wait
+  const bool producer = warp == 0 && lane == 0;
+  if (!producer) {
+    griddep_wait();
+    griddep_launch_dependents();
+  }
 
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
       bool ok = true;
-      for (int i = 0; i < nk; ++i) {
+      auto load_w = [&](int i) {
         const int s = i % S;
-        const uint32_t ph = (uint32_t)(i / S) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, p.err)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&full[s], kABytes + b_bytes);
         // rotated K order: concurrently running CTAs read different X blocks
         const int kc = (kb0 + (i + rot) % nk) * kGemmBK;
         if (p.epi == EPI_SILU) {
@@ -432,7 +431,32 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         } else {
           tma_load_2d(a_smem + (size_t)s * kABytes, &tmW, &full[s], kc, n0);
         }
-        tma_load_2d(b_smem + (size_t)s * b_bytes, &tmX, &full[s], kc, t0);
+      };
+      auto load_x = [&](int i) {
+        const int s = i % S;
+        tma_load_2d(b_smem + (size_t)s * b_bytes, &tmX, &full[s], (kb0 + (i + rot) % nk) * kGemmBK, t0);
+      };
+      // the first pass over the ring needs no empty wait: weights first, then
+      // (after the previous kernel) the activations of those stages
+      const int pre = min(S, nk);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], kABytes + b_bytes);
+        load_w(i);
+      }
+      griddep_wait();
+      griddep_launch_dependents();
+      for (int i = 0; i < pre; ++i) load_x(i);
+      issued = pre;
+      for (int i = pre; i < nk; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (uint32_t)(i / S) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, p.err)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], kABytes + b_bytes);
+        load_w(i);
+        load_x(i);
         ++issued;
       }
       if (!ok) {

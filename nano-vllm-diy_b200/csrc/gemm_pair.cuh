@@ -309,30 +309,65 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // everything above overlaps the previous kernel's tail (programmatic
-  // dependent launch); activations and the stream-K workspace are used below
-  griddep_wait();
-  griddep_launch_dependents();
+  // dependent launch), and so do the producer's weight loads for the first
+  // ring stages (weights are parameters; no kernel of the step writes them);
+  // activations, outputs and the split-K workspace are touched only after
+  // the wait
+  const bool producer = warp == 0 && lane == 0;
+  if (!producer) {
+    griddep_wait();
+    griddep_launch_dependents();
+  }
 
   if (warp == 0) {
     // ---- producer (both CTAs): this CTA's 128 tokens and NP/2 weight rows
     if (lane == 0) {
       const uint32_t full_leader = map_to_rank(smem_u32(full), leader);
+      auto weight_row = [&](long long tile) {
+        // plain: features mt*NP + v*NP/2; SiLU: gate rows (leader) or the
+        // matching up rows (peer) of features mt*128
+        const int mt = (int)(tile / p.tiles_t);
+        return silu ? (int)v * p.silu_inter + mt * 128 : mt * NP + (int)v * (NP / 2);
+      };
       int it = 0;
       bool ok = true;
       long long su = u_begin;
       int sk = 0;
       PairSeg sg;
+      // the first pass over the ring needs no empty wait: the first
+      // segment's weights first, the activations of those stages after the
+      // previous kernel
+      int pre = 0;
+      {
+        long long su0 = u_begin;
+        int sk0 = 0;
+        PairSeg s0;
+        if (next_seg(su0, sk0, s0)) {
+          const int wrow = weight_row(s0.tile);
+          pre = min(S, s0.kbe - s0.kbb);
+          for (int j = 0; j < pre; ++j) {
+            if (v == 0) mbar_arrive_expect_tx(&full[j], 2u * (kABytes + b_bytes));
+            tma_load_2d_pair(smem_u32(b_smem + (size_t)j * b_bytes), &tmW, full_leader + (uint32_t)j * 8u,
+                             (s0.kbb + j) * kGemmBK, wrow);
+          }
+        }
+      }
+      griddep_wait();
+      griddep_launch_dependents();
       while (ok && next_seg(su, sk, sg)) {
         const int kbb = sg.kbb, kbe = sg.kbe;
         const int mt = (int)(sg.tile / p.tiles_t);
         const int tt = (int)(sg.tile - (long long)mt * p.tiles_t);
         const int tok = tt * 2 * kGemmBM + (int)v * kGemmBM;
-        // weight rows: plain = features mt*NP + v*NP/2; SiLU = gate rows
-        // (leader) or the matching up rows (peer) of features mt*128
-        const int wrow = silu ? (int)v * p.silu_inter + mt * 128 : mt * NP + (int)v * (NP / 2);
+        const int wrow = weight_row(sg.tile);
         for (int kb = kbb; kb < kbe; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (uint32_t)(it / S) & 1u;
+          if (it < pre) {  // weights already in flight: the activations now
+            tma_load_2d_pair(smem_u32(a_smem + (size_t)s * kABytes), &tmX, full_leader + (uint32_t)s * 8u,
+                             kb * kGemmBK, tok);
+            continue;
+          }
           if (!mbar_wait(&empty[s], ph ^ 1u, p.err)) {
             ok = false;
             break;
