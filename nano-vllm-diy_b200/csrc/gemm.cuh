@@ -77,10 +77,11 @@ struct GemmArgs {
   long long ldy;       // row stride of y (elements)
   const __nv_bfloat16* bias;  // [N] or nullptr (EPI_BF16 only)
   int silu_inter;      // EPI_SILU: I (rows of W are [gate(I) ; up(I)])
-  // stream-K schedule of the persistent SM-pair kernel
+  // split-K state of the persistent SM-pair kernel (both schedules)
   int tiles_m;         // 256-row weight tiles (pairs of 128-row CTA tiles)
   int tiles_t;         // token tiles of BN
-  unsigned* sk_flags;  // [pairs * 2] partial-ready flags (zero between launches)
+  unsigned* sk_flags;  // [pairs * 2] partial-ready flags, then the grouped schedule's done
+                       // counters at word kGrpDoneOffset (all zero between launches)
   float* sk_part;      // [pairs * 2][BN][128] fp32 partial tiles
   int use_tma_store;   // outputs written by TMA tensor stores (needs y 16-byte aligned, ldy % 8 == 0)
   // schedule of the SM-pair kernel: 0 stream-K over the flat (tile, K block)

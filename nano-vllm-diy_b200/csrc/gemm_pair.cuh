@@ -138,7 +138,7 @@ __device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs
 }
 
 // ---------------------------------------------------------------------------
-// Persistent SM-pair GEMM with a stream-K schedule.
+// Persistent SM-pair GEMM with a grouped split-K or a stream-K schedule.
 //
 // Operand roles: the TOKENS are the M = 256 operand (128 per CTA of the pair,
 // TMEM lane = token) and the weight rows the N operand (the pair's NP
@@ -147,11 +147,13 @@ __device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs
 // for the gate_up projection a tile's columns are [128 gate | the 128
 // matching up rows], so SiLU-and-mul needs no exchange between threads.
 //
-// grid = 2 x pairs CTAs (all co-resident), cluster (2, 1, 1).  The work is
-// the flat sequence of (tile, K block) units, tile = (feature tile m, token
-// tile t) with t fastest (tiles sharing weights run back to back); pair p
-// takes units [total p / P, total (p+1) / P).  A range cuts tiles into
-// segments:
+// grid = 2 x pairs CTAs (all co-resident), cluster (2, 1, 1); tile =
+// (feature tile m, token tile t) with t fastest (tiles sharing weights run
+// back to back).
+//
+// Stream-K schedule (p.sched = 0): the work is the flat sequence of (tile, K
+// block) units; pair p takes units [total p / P, total (p+1) / P).  A range
+// cuts tiles into segments:
 //   whole        all K blocks of a tile       -> epilogue writes the output
 //   contributor  first segment of a range that starts inside a tile (its
 //                tail K blocks)               -> fp32 partial to sk_part[p],

@@ -7,7 +7,7 @@ fallback: if the shared library is missing or a tensor is not on a CUDA
 device, the call fails.
 
 The decode-attention workspace (its scheduler counters and split-KV partials)
-and the GEMM workspace (stream-K flags and fp32 partials of the SM-pair GEMM)
+and the GEMM workspace (split-K flags and fp32 partials of the SM-pair GEMM)
 are per-device torch buffers that grow on demand outside CUDA-graph capture
 and are reused by every call.
 """
@@ -176,7 +176,7 @@ _gemm_ws_bytes: dict[int, int] = {}
 
 
 def _gemm_workspace(device: torch.device) -> torch.Tensor:
-    """The GEMM's stream-K workspace of this device (zeroed on allocation,
+    """The GEMM's split-K workspace of this device (zeroed on allocation,
     sized before any graph capture by the first eager call)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     n = _gemm_ws_bytes.get(idx)
