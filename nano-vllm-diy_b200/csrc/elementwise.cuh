@@ -28,11 +28,19 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
                                                        long long out_stride,
                                                        __nv_bfloat16* __restrict__ res_out,
                                                        int dim, float eps) {
-  griddep_wait();
-  griddep_launch_dependents();
   __shared__ float s_red[8];
   const int row = blockIdx.x;
   const int nvec = dim / 8;
+  // the norm weights are parameters (no kernel of the step writes them): their
+  // loads are issued first and overlap the previous kernel and the row loads
+  uint4 wv[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    wv[i] = vi < nvec ? *reinterpret_cast<const uint4*>(w + vi * 8) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  griddep_wait();
+  griddep_launch_dependents();
   float v[VPT][8];
   float ss = 0.f;
 #pragma unroll
@@ -77,8 +85,7 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __re
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
-      const uint4 wr = *reinterpret_cast<const uint4*>(w + vi * 8);
-      const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wr);
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wv[i]);
       uint4 packed;
       uint32_t* pk = reinterpret_cast<uint32_t*>(&packed);
 #pragma unroll
