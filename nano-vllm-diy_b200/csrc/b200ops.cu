@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "attention.cuh"
@@ -28,6 +29,11 @@ using namespace b200;
 namespace {
 
 thread_local std::string g_last_error;
+
+// Guards the host-side per-device state and lookup caches below (filled on
+// first use; several host threads may drive the library).  Taken only in
+// leaf functions, which never call one another while holding it.
+std::mutex g_host_mutex;
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -101,6 +107,7 @@ DeviceState g_dev[kMaxDevices];
 __device__ unsigned g_device_error_word;
 
 int device_state(DeviceState** out) {
+  std::lock_guard<std::mutex> lock(g_host_mutex);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
@@ -124,6 +131,7 @@ int device_state(DeviceState** out) {
 template <typename K>
 int ensure_smem(DeviceState* ds, unsigned bit, K kernel, int bytes) {
   static int configured[kMaxDevices][8] = {};
+  std::lock_guard<std::mutex> lock(g_host_mutex);
   int dev = 0;
   cudaGetDevice(&dev);
   int slot = 0;
@@ -138,6 +146,7 @@ int ensure_smem(DeviceState* ds, unsigned bit, K kernel, int bytes) {
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::lock_guard<std::mutex> lock(g_host_mutex);
   if (fn == nullptr) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -151,6 +160,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 PFN_cuMemGetAddressRange_v3020 address_range_fn() {
   static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  std::lock_guard<std::mutex> lock(g_host_mutex);
   if (fn == nullptr) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -357,6 +367,7 @@ PairSchedule pair_schedule(long long tiles, int num_kb, int max_pairs, bool allo
 long long pair_resident(int splits, int smem) {
   static long long cache[kMaxDevices][5][4] = {};
   static int cache_smem[kMaxDevices][5][4] = {};
+  std::lock_guard<std::mutex> lock(g_host_mutex);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices || splits < 1 || splits > 4) return 0;
@@ -598,6 +609,7 @@ int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ld
   int dev_id = 0;
   cudaGetDevice(&dev_id);
   auto resident_for = [&](int splits) -> long long {
+    std::lock_guard<std::mutex> lock(g_host_mutex);
     for (int i = 0; i < 4; ++i)
       if (resident_smem[dev_id][splits][i] == p.smem) return resident_cache[dev_id][splits][i];
     const long long v = [&]() -> long long {
@@ -1075,6 +1087,7 @@ static __device__ __align__(256) unsigned char g_static_decode_scratch[kStaticDe
 // device (host code may not use the symbol itself as a device pointer).
 int static_decode_scratch(void** out) {
   static void* addr[kMaxDevices] = {};
+  std::lock_guard<std::mutex> lock(g_host_mutex);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
