@@ -321,6 +321,31 @@ def test_decode_attention_long_and_repeated():
     assert torch.equal(out1, out2)
 
 
+def test_decode_attention_mix_alternating_batches():
+    """A serving-like mix (about 100 sequences of 100-2100 keys: most are split
+    into 2-5 items and merged) on 512-key pages, three calls alternating two
+    batches in one workspace: the per-(sequence, kv head) completion counters
+    and both queues must come back to zero after every call."""
+    import random
+    from src import b200
+    rng = random.Random(7)
+    scale = 128 ** -0.5
+    cases = []
+    for seed in (41, 42):
+        lens_k = [rng.randint(100, 2100) for _ in range(120 if seed == 41 else 97)]
+        q, kc, vc, bt, cu_q, cu_k = _paged_case([1] * len(lens_k), lens_k, 32, 8, page=512, seed=seed)
+        ref = L.varlen_attention(q, None, None, cu_q, cu_k, scale, kc, vc, bt)
+        args = (q.to(DEV), None, None, kc.to(DEV), vc.to(DEV), cu_q.to(DEV), cu_k.to(DEV), 1,
+                max(lens_k), scale, bt.to(DEV))
+        cases.append((args, ref))
+    for i in (0, 1, 0):
+        args, ref = cases[i]
+        out = b200.paged_attention(*args)
+        torch.cuda.synchronize()
+        assert L.rel_err(out.cpu(), ref) <= 2e-2, i
+    assert b200.device_error(clear=True) == 0
+
+
 def test_decode_attention_graph_padding():
     """CUDA-graph replay pads cu_seqlens with 0 and block tables with -1
     (src/engine/model_runner.py:248-257): padded rows must be skipped."""
