@@ -231,8 +231,8 @@ int make_tmap_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
 // ---------------------------------------------------------------------------
 struct GemmPlan {
   int BN, token_tiles, n_tiles, num_kb, kb_per_split, splits, stages, smem, tmem_cols;
-  // SM-pair kernel schedule (GemmArgs::sched, grp_*)
-  int sched, grp_whole, grp_split, grp_size;
+  // SM-pair kernel schedule (GemmArgs::sched, grp_*, csplit)
+  int sched, grp_whole, grp_split, grp_size, csplit;
 };
 
 int round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -327,6 +327,13 @@ bool pair_forced() {
   const char* e = getenv("B200_GEMM_PAIR");
   return e && *e == '2';
 }
+// B200_GEMM_PAIR=3: the SM-pair kernel's cluster split-K mode for plain
+// (non-SiLU) GEMMs.
+bool csk_forced() {
+  const char* e = getenv("B200_GEMM_PAIR");
+  return e && *e == '3';
+}
+
 bool grouped_allowed() {
   const char* e = getenv("B200_GEMM_SCHED");
   return !(e && std::strcmp(e, "streamk") == 0);
@@ -444,6 +451,51 @@ GemmPlan plan_pair(DeviceState* ds, int T, int N, int K, bool silu_tiles, int* r
   return p;
 }
 
+// Plan of the pair kernel's cluster split-K mode (plain GEMMs): clusters of 2
+// pairs, one tile each, K halves.  NP = the smallest multiple of 32 (<= 256)
+// whose tiles all fit the co-resident clusters of 4 CTAs (more tiles keep more
+// SMs busy; 256 and waves of clusters when none fits).  `splits` = pairs
+// launched (2 per tile), 0 when the mode does not apply; *resident tells
+// whether every cluster is co-resident.
+GemmPlan plan_pair_cluster(DeviceState* ds, int T, int N, int K, bool* resident, int* rc) {
+  GemmPlan best{};
+  *rc = 0;
+  *resident = false;
+  const int num_kb = (K + kGemmBK - 1) / kGemmBK;
+  if (num_kb < 2) return best;
+  const int token_tiles = (T + 2 * kGemmBM - 1) / (2 * kGemmBM);
+  for (int np = 32; np <= 256; np += 32) {
+    GemmPlan p{};
+    p.BN = np;
+    p.token_tiles = token_tiles;
+    p.n_tiles = 2 * ((N + np - 1) / np);
+    p.num_kb = num_kb;
+    const int stage = kGemmBM * kGemmBK * 2 + (np / 2) * kGemmBK * 2;
+    const int extra = 4 * kGemmBM * 64 + 512;
+    p.stages = std::min(kGemmMaxStages, (kPairSmemBudget - 1024 - extra) / stage);
+    p.smem = 1024 + p.stages * stage + extra;
+    int cols = 32;
+    while (cols < np) cols <<= 1;
+    p.tmem_cols = 2 * cols;
+    // the ring receives the other member's partial of ceil(NP/32 / 2) chunks
+    if ((long long)p.stages * stage < (long long)((np / 32 + 1) / 2) * kChunkFloats * 4) continue;
+    if ((*rc = ensure_smem(ds, 8u, gemm_pair_tcgen05_kernel, p.smem))) return best;
+    const long long tiles = (long long)(p.n_tiles / 2) * token_tiles;
+    p.sched = 0;
+    p.csplit = 2;
+    p.splits = (int)(2 * tiles);
+    best = p;
+    if (tiles * 4 <= pair_resident(2, p.smem)) {  // every cluster resident at once
+      *resident = true;
+      break;
+    }
+  }
+  if (gemm_debug() && best.splits)
+    fprintf(stderr, "[b200 gemm pair] T=%d N=%d K=%d NP=%d tiles=%d kb=%d cluster split-K pairs=%d smem=%d\n", T,
+            N, K, best.BN, best.n_tiles / 2 * best.token_tiles, best.num_kb, best.splits, best.smem);
+  return best;
+}
+
 int launch_pair(const GemmPlan& p, const CUtensorMap& tmW, const CUtensorMap& tmX,
                 const CUtensorMap& tmY, const GemmArgs& a, cudaStream_t st, const char* what) {
   cudaLaunchConfig_t cfg = {};
@@ -453,7 +505,7 @@ int launch_pair(const GemmPlan& p, const CUtensorMap& tmW, const CUtensorMap& tm
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.x = p.csplit == 2 ? 4 : 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -489,13 +541,32 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
   const bool use_pair = pair_enabled() && workspace != nullptr && aligned16(workspace) &&
                         ws_bytes >= pair_workspace_bytes(ds->num_sms) &&
                         (pair_forced() || pair_tiles >= ds->num_sms / 2);
+  // The pair kernel's cluster split-K mode also takes plain GEMMs with more
+  // than 128 tokens and fewer tiles than pairs when its tiles stay at least
+  // 192 rows wide with every cluster resident (measured: qkv 6144 x 4096 at
+  // T = 256 22.8 us against 24.5; with 128-row tiles the token bytes each SM
+  // reads outweigh the on-chip reduction: o_proj even, down 48.8 against 38.2).
   GemmPlan pp{};
-  if (use_pair) {
+  bool pair = use_pair;
+  const bool csk_ok = !silu && pair_enabled() && workspace != nullptr && aligned16(workspace) &&
+                      ws_bytes >= pair_workspace_bytes(ds->num_sms);
+  bool csk_used = false;
+  if (csk_ok && (csk_forced() || (!use_pair && T > kGemmBM))) {
+    int prc = 0;
+    bool resident = false;
+    const GemmPlan cp = plan_pair_cluster(ds, T, N, K, &resident, &prc);
+    if (prc) return prc;
+    if (cp.splits > 0 && (csk_forced() || (resident && cp.BN >= 192))) {
+      pp = cp;
+      pair = csk_used = true;
+    }
+  }
+  if (!csk_used && use_pair) {
     int prc = 0;
     pp = plan_pair(ds, T, N, K, silu, &prc);
     if (prc) return prc;
   }
-  if (use_pair) {
+  if (pair) {
     const GemmPlan& p = pp;
     CUtensorMap tmW, tmX;
     if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK,
@@ -520,6 +591,7 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
     a.grp_whole = p.grp_whole;
     a.grp_split = p.grp_split;
     a.grp_size = p.grp_size;
+    a.csplit = p.csplit;
     a.err = ds->err;
     // outputs by TMA tensor stores: box of 32 features x 128 tokens, 64-byte
     // swizzle (the kernel's staging layout)

@@ -122,6 +122,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// Bounded wait with cluster-scope acquire: for phases completed by other CTAs'
+// st.async writes (their data is visible to this thread once it returns).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned* err) {
+  const uint32_t addr = smem_u32(bar);
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_error(err, ERR_MBAR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// 16-byte store into another CTA's shared memory (shared::cluster address)
+// whose completion is counted, in bytes, on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_v4(uint32_t dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                            uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   dst),
+               "r"(a), "r"(b), "r"(c), "r"(d), "r"(bar)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tiled loads into this CTA's own shared memory)
 // ---------------------------------------------------------------------------
@@ -175,6 +207,14 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 // memory writes before it with the distributed reads after it.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of cluster_sync, for threads that have other work between
+// arriving and needing every CTA's arrival.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Address of the same shared-memory location in CTA `rank` of the cluster.

@@ -91,6 +91,8 @@ struct GemmArgs {
   // grp_split + p + j * pairs
   int sched;
   int grp_whole, grp_split, grp_size;
+  int csplit;          // 2: cluster split-K (clusters of 2 pairs, one tile each, K halves
+                       // reduced through distributed shared memory); 0: off
   unsigned* err;
   AllReducePeers ar;   // EPI_ALLREDUCE only
 };

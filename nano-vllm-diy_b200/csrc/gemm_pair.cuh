@@ -179,6 +179,15 @@ __device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs
 // members' partials and writes them.  The reduction is spread over all
 // members, and for w >= 1 it overlaps the MMAs of the next whole tile.  The
 // last member to finish resets the group's flags for the next launch.
+//
+// Cluster split-K (p.csplit = 2; plain epilogue only): clusters of 4 CTAs =
+// 2 pairs and one tile per cluster; member m = cluster rank / 2 computes K
+// blocks [m nkb / 2, (m + 1) nkb / 2).  Member m owns the 32-wide output
+// chunks c with c % 2 == m.  After a cluster barrier (every ring of the
+// cluster is idle) each CTA pushes the chunks the other member owns from
+// TMEM straight into that member's stage ring (st.async, counted on its
+// mbarrier), then sums its own chunks from TMEM and the pushed partials and
+// writes them: no L2 round trip and no flags.
 // ---------------------------------------------------------------------------
 
 // One segment of a pair's work: K blocks [kbb, kbe) of `tile`; `member` is
@@ -274,9 +283,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int pairs = gridDim.x >> 1;
   const long long tiles = (long long)p.tiles_m * p.tiles_t;
   const long long total = tiles * p.num_kb;
-  // stream-K: this pair's units (unused by the grouped schedule)
-  const long long u_begin = sk_begin(total, pr, pairs);
-  const long long u_end = sk_begin(total, pr + 1, pairs);
+  const bool csk = p.csplit == 2;     // cluster split-K
+  const int cmem = (int)(crank >> 1);  // cluster split-K: member index (0, 1)
+  // stream-K: this pair's units (unused by the grouped schedule); cluster
+  // split-K: this member's half of the cluster's tile (one segment)
+  long long u_begin, u_end;
+  if (csk) {
+    const long long t0 = (long long)(blockIdx.x >> 2) * p.num_kb;
+    u_begin = t0 + (long long)cmem * p.num_kb / 2;
+    u_end = t0 + (long long)(cmem + 1) * p.num_kb / 2;
+  } else {
+    u_begin = sk_begin(total, pr, pairs);
+    u_end = sk_begin(total, pr + 1, pairs);
+  }
   auto next_seg = [&](long long& u, int& k, PairSeg& sg) {
     return pair_next_seg(p.sched, tiles, p.num_kb, p.grp_whole, p.grp_split, p.grp_size, pr, pairs, u,
                          u_end, k, sg);
@@ -387,6 +406,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, p.err);
       }
     }
+    if (csk) cluster_arrive();  // this warp is done with the ring (cluster split-K)
   } else if (warp == 1) {
     // ---- MMA issuer (leader only): M = 256 tokens, N = NP columns
     if (lane == 0 && v == 0) {
@@ -429,6 +449,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_commit_pair(accf_peer + (uint32_t)b * 8u);
       }
     }
+    if (csk) cluster_arrive();  // this warp is done with the ring (cluster split-K)
   } else {
     // ---- epilogue warps 2..5: TMEM lane quarters 2,3,0,1; thread = token
     const int q = warp & 3;
@@ -483,7 +504,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     };
-    long long su = u_begin;
+    if (csk) {
+      // ---- cluster split-K (see the schedule notes above).  The other
+      // member pushes its partial of this CTA's output chunks (c % 2 == cmem)
+      // into ring slots c / 2: arm the byte count before the barrier.
+      const int n_own = (nchunks - cmem + 1) / 2;
+      if (lead_thread) mbar_arrive_expect_tx(&fix_bar[0], (uint32_t)n_own * kChunkFloats * 4);
+      const bool have = mbar_wait(&acc_full[0], 0u, p.err);
+      tc_fence_before();
+      cluster_arrive();
+      cluster_wait();  // every pair of the cluster has finished its MMAs: every ring is idle
+      tc_fence_after();
+      const uint32_t d = tmem_base + ((uint32_t)(q * 32) << 16);
+      const uint32_t peer = (uint32_t)((1 - cmem) * 2) + v;  // the other member, same token half
+      const uint32_t peer_ring = map_to_rank(smem_u32(smem), peer) + (uint32_t)row * 16u;
+      const uint32_t peer_bar = map_to_rank(smem_u32(&fix_bar[0]), peer);
+      for (int c = 1 - cmem; c < nchunks; c += 2) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(d + (uint32_t)(c * 32), r);
+        tmem_ld_wait_regs(r);
+        const uint32_t dst = peer_ring + (uint32_t)(c / 2) * (uint32_t)(kChunkFloats * 4);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          st_async_v4(dst + (uint32_t)(j * kGemmBM * 16), r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3],
+                      peer_bar);
+      }
+      const bool got = mbar_wait_cluster(&fix_bar[0], 0u, p.err);
+      const long long tile = blockIdx.x >> 2;
+      const int mt = (int)(tile / p.tiles_t);
+      const int tt = (int)(tile - (long long)mt * p.tiles_t);
+      const int row0 = tt * 2 * kGemmBM + (int)v * kGemmBM;
+      const int tok = row0 + row;
+      for (int c = cmem; c < nchunks; c += 2) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(d + (uint32_t)(c * 32), r);
+        tmem_ld_wait_regs(r);
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = have ? __uint_as_float(r[j]) : 0.f;
+        if (got) {
+          // own + other member (fp32 addition commutes: the same sum on both owners)
+          const float4* src = reinterpret_cast<const float4*>(smem + (size_t)(c / 2) * kChunkFloats * 4) + row;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 f = src[j * kGemmBM];
+            acc[4 * j] += f.x; acc[4 * j + 1] += f.y; acc[4 * j + 2] += f.z; acc[4 * j + 3] += f.w;
+          }
+        }
+        const int f0 = mt * NP + c * 32;
+        if (p.bias != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (f0 + j < p.N) acc[j] += __bfloat162float(p.bias[f0 + j]);
+        }
+        emit_chunk(acc, f0, p.N, row0, tok);
+      }
+    }
+    long long su = csk ? u_end : u_begin;  // cluster split-K: no segment loop
     int sk = 0;
     PairSeg sg;
     for (; next_seg(su, sk, sg); ++seg) {
@@ -853,6 +930,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     if (lead_thread && p.use_tma_store) bulk_wait_group_all();  // outputs written before exit
   }
+  // the producer and MMA warps complete the cluster barrier they arrived on
+  if (csk && warp < 2) cluster_wait();
   // every TMEM read and remote arrive of both CTAs is done before the pair
   // frees its TMEM and either CTA exits
   tc_fence_before();

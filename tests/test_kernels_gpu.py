@@ -52,7 +52,7 @@ def test_linear(T, N, K):
 
 @pytest.mark.parametrize("kernel,pairs", [("grouped", ""), ("grouped", "1"), ("grouped", "3"),
                                           ("grouped", "17"), ("streamk", ""), ("streamk", "3"),
-                                          ("streamk", "17"), ("single", "")])
+                                          ("streamk", "17"), ("cluster", ""), ("single", "")])
 @pytest.mark.parametrize("T,N,K", [(256, 4096, 4096), (77, 1280, 2048), (513, 768, 1024),
                                    (256, 24576, 1024), (256, 6144, 4096)])
 def test_linear_kernels_and_splits(T, N, K, kernel, pairs, monkeypatch):
@@ -60,9 +60,11 @@ def test_linear_kernels_and_splits(T, N, K, kernel, pairs, monkeypatch):
     SM-pair kernel (tcgen05.mma.cta_group::2) with its grouped split-K
     schedule (whole tiles only, split tiles only, both) and with its
     stream-K schedule (whole tiles, contributor / finisher segments),
-    whatever number of pairs shares the work, and the single-SM kernel."""
+    whatever number of pairs shares the work, the same kernel's cluster
+    split-K mode (plain GEMM; the SiLU call takes the default path), and the
+    single-SM kernel."""
     from src import b200
-    monkeypatch.setenv("B200_GEMM_PAIR", "0" if kernel == "single" else "2")
+    monkeypatch.setenv("B200_GEMM_PAIR", {"single": "0", "cluster": "3"}.get(kernel, "2"))
     monkeypatch.setenv("B200_GEMM_SCHED", "streamk" if kernel == "streamk" else "")
     monkeypatch.setenv("B200_GEMM_PAIRS", pairs)
     x = randn(T, K, seed=11)
@@ -76,13 +78,13 @@ def test_linear_kernels_and_splits(T, N, K, kernel, pairs, monkeypatch):
     assert b200.device_error(clear=True) == 0
 
 
-@pytest.mark.parametrize("kernel,T", [("default", 48), ("grouped", 200), ("streamk", 200)])
+@pytest.mark.parametrize("kernel,T", [("default", 48), ("grouped", 200), ("streamk", 200), ("cluster", 200)])
 @pytest.mark.parametrize("col0", [0, 1])
 def test_linear_bias_and_strided_out(kernel, T, col0, monkeypatch):
     """Bias and an output view with a row stride wider than N; col0 = 1 makes
     the rows 2-byte aligned only, so the kernels store without TMA."""
     from src import b200
-    monkeypatch.setenv("B200_GEMM_PAIR", "1" if kernel == "default" else "2")
+    monkeypatch.setenv("B200_GEMM_PAIR", {"default": "1", "cluster": "3"}.get(kernel, "2"))
     monkeypatch.setenv("B200_GEMM_SCHED", "streamk" if kernel == "streamk" else "")
     N, K = 640, 1024
     x = randn(T, K, seed=3)
