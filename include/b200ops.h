@@ -81,8 +81,8 @@ int b200_gemm_schedule_check(long long tiles, int num_kb, int max_pairs, int gro
  * K, ldx and ldw must be multiples of 8; x and w 16-byte aligned.
  * With a workspace of b200_linear_workspace_bytes() bytes (zeroed once,
  * 16-byte aligned) the GEMM runs on the persistent SM-pair kernel
- * (tcgen05.mma.cta_group::2; grouped split-K or stream-K schedule) where
- * that is faster; with NULL it runs on the single-SM kernel.  Concurrent
+ * (tcgen05.mma.cta_group::2; grouped split-K, stream-K or cluster split-K
+ * schedule) where that is faster; with NULL it runs on the single-SM kernel.  Concurrent
  * calls must not share one workspace. */
 int b200_linear(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
                 void* y, long long ldy, int T, int N, int K, void* workspace, size_t ws_bytes,
