@@ -68,3 +68,34 @@ def test_gemm_schedule_partitions_the_work():
                     cases += 1
     assert cases > 1000
     assert lib.b200_gemm_schedule_check(0, 64, 74, 1) < 0
+
+
+def test_every_python_op_refuses_cpu_tensors():
+    """The product path has no CPU fallback: each op of the binding raises on
+    CPU tensors before it reaches the library (no launch, no silent torch
+    substitute)."""
+    import pytest
+    import torch
+    from src import b200
+    bf = torch.bfloat16
+    x = torch.zeros(4, 64, dtype=bf)
+    w = torch.zeros(128, 64, dtype=bf)
+    q = torch.zeros(4, 2, 128, dtype=bf)
+    kv = torch.zeros(4, 1, 128, dtype=bf)
+    cache = torch.zeros(2, 256, 1, 128, dtype=bf)
+    i32 = torch.zeros(5, dtype=torch.int32)
+    calls = [
+        lambda: b200.linear(x, w),
+        lambda: b200.linear_silu_and_mul(x, w),
+        lambda: b200.rms_norm(x, torch.zeros(64, dtype=bf), 1e-6),
+        lambda: b200.silu_and_mul(x),
+        lambda: b200.store_kvcache(kv, kv, cache, cache, torch.zeros(4, dtype=torch.int32)),
+        lambda: b200.qk_norm_rope_store(q, kv, kv, None, None, 1e-6, torch.zeros(16, 128),
+                                        torch.zeros(4, dtype=torch.int64)),
+        lambda: b200.paged_attention(q, kv, kv, None, None, i32, i32, 1, 4, 0.1),
+        lambda: b200.embedding(torch.zeros(4, dtype=torch.int64), w, 0, 128),
+        lambda: b200.argmax(x),
+    ]
+    for call in calls:
+        with pytest.raises(RuntimeError, match="CUDA tensors"):
+            call()
