@@ -322,9 +322,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
 // ---------------------------------------------------------------------------
 // cp.async / ldmatrix / mma.sync (attention kernels)
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
 __device__ __forceinline__ void cp_async_16_zfill(uint32_t dst, const void* src, bool valid) {
   const int n = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
