@@ -146,14 +146,21 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 # CPU side: the oracle port of the reference path
 # --------------------------------------------------------------------------
-class CpuDecodeSample:
+class CpuDecodeStep:
     """The oracle (the reference's torch path restated for the CPU) on the host
-    cores: one Qwen3-8B decoder layer over `n_seqs` decode sequences of the
-    mix, plus the LM head for those tokens.  GEMMs use torch's bf16 F.linear,
-    the op the reference calls.  tok/s = n_seqs / (36 x layer time + head
-    time): an extrapolation from one layer, stated in the sample text."""
+    cores, on the bench's own workload: one greedy decode step of the 256
+    sequences of the mix through all 36 Qwen3-8B decoder layers, the final
+    norm, the LM head over the full 151936-entry vocabulary and the argmax.
+    GEMMs use torch's bf16 F.linear, the op the reference calls
+    (src/layers/linear.py:75,170; src/layers/llm_head.py:64).
 
-    def __init__(self, n_seqs: int = 8, seed: int = 0):
+    Host memory is kept to a few GB: all 36 layers reference the same random
+    layer weights (436 MB, far larger than any CPU cache, so no layer finds
+    another's weights cached) and the same paged K/V tensors, which hold the
+    whole mix (1 GB).  The arithmetic of a step is exactly that of a step of
+    the model; only the values differ."""
+
+    def __init__(self, seed: int = 0, batch: int = 256):
         from oracle import layers as L
         from oracle import model as OM
         from oracle.weights import random_weights
@@ -161,89 +168,115 @@ class CpuDecodeSample:
         torch.set_num_threads(os.cpu_count() or 1)
         L.NATIVE_BF16_LINEAR = True
         self.L, self.OM = L, OM
-        self.full = qwen3_8b_config()
-        self.one = dataclasses.replace(self.full, layers=1)
-        # random weights for the layer; the 151936-row embedding / LM head are a
-        # small random block tiled to full size (their values do not change
-        # the CPU time, and drawing 1.2 G normals would dominate the setup)
-        self.W = random_weights(dataclasses.replace(self.one, vocab=4096), seed=seed)
+        self.shape = qwen3_8b_config()
+        one = dataclasses.replace(self.shape, layers=1, vocab=4096)
+        W = random_weights(one, seed=seed)
+        p0 = "model.layers.0."
+        W[p0 + "self_attn.qkv_proj.weight"] = torch.cat(
+            [W[p0 + "self_attn.q_proj.weight"], W[p0 + "self_attn.k_proj.weight"],
+             W[p0 + "self_attn.v_proj.weight"]], 0)
+        W[p0 + "mlp.gate_up_proj.weight"] = torch.cat(
+            [W[p0 + "mlp.gate_proj.weight"], W[p0 + "mlp.up_proj.weight"]], 0)
+        layer0 = {k[len(p0):]: v for k, v in W.items() if k.startswith(p0)}
+        for i in range(1, self.shape.layers):
+            for k, v in layer0.items():
+                W[f"model.layers.{i}.{k}"] = v
+        # full-size embedding and LM head: a random block tiled to 151936 rows
+        # (drawing 1.2 G normals would dominate the set-up; the values do not
+        # change the CPU time)
         for name in ("model.embed_tokens.weight", "lm_head.weight"):
-            small = self.W[name]
-            reps = (self.full.vocab + small.shape[0] - 1) // small.shape[0]
-            self.W[name] = small.repeat(reps, 1)[:self.full.vocab].contiguous()
-        self.n = n_seqs
-        self.lens = mix(256, seed)[:n_seqs]
-        nblk = sum((n + BLOCK - 1) // BLOCK for n in self.lens)
-        self.kv = OM.OracleKV(self.one, nblk, BLOCK)
+            small = W[name]
+            reps = (self.shape.vocab + small.shape[0] - 1) // small.shape[0]
+            W[name] = small.repeat(reps, 1)[:self.shape.vocab].contiguous()
+        self.W = W
+        self.n = batch
+        self.lens = mix(256, seed)[:batch]
+        pages = [(n + BLOCK - 1) // BLOCK for n in self.lens]
+        nblk = sum(pages)
+        kv = OM.OracleKV(one, nblk, BLOCK)
         g = torch.Generator().manual_seed(seed)
-        self.kv.k[0].copy_(torch.randn(self.kv.k[0].shape, generator=g).to(torch.bfloat16))
-        self.kv.v[0].copy_(torch.randn(self.kv.v[0].shape, generator=g).to(torch.bfloat16))
-        bt = torch.full((n_seqs, max((n + BLOCK - 1) // BLOCK for n in self.lens)), -1,
-                        dtype=torch.int32)
-        nxt = 0
-        for i, n in enumerate(self.lens):
-            for j in range((n + BLOCK - 1) // BLOCK):
-                bt[i, j] = nxt
-                nxt += 1
+        # N(0, 1) K/V (as on the GPU side): a 64 Mi-element random block tiled
+        for t in (kv.k[0], kv.v[0]):
+            flat = t.view(-1)
+            blk = torch.randn(min(flat.numel(), 1 << 26), generator=g).to(torch.bfloat16)
+            for o in range(0, flat.numel(), blk.numel()):
+                m = min(blk.numel(), flat.numel() - o)
+                flat[o:o + m].copy_(blk[:m])
+        kv.k = kv.k * self.shape.layers
+        kv.v = kv.v * self.shape.layers
+        self.kv = kv
+        perm = np.random.default_rng(seed).permutation(nblk)
+        bt = torch.full((batch, max(pages)), -1, dtype=torch.int32)
+        k = 0
+        for i, n in enumerate(pages):
+            bt[i, :n] = torch.from_numpy(perm[k:k + n].astype(np.int32))
+            k += n
         self.pos = torch.tensor([n - 1 for n in self.lens], dtype=torch.int64)
-        slots = torch.tensor([int(bt[i, (n - 1) // BLOCK]) * BLOCK + (n - 1) % BLOCK
-                              for i, n in enumerate(self.lens)], dtype=torch.int32)
-        self.ctx = dict(cu_seqlens_q=torch.arange(n_seqs + 1, dtype=torch.int32),
-                        cu_seqlens_k=torch.tensor([0] + list(np.cumsum(self.lens)), dtype=torch.int32),
+        slots = (bt.long().gather(1, (self.pos // BLOCK)[:, None])[:, 0] * BLOCK
+                 + self.pos % BLOCK).to(torch.int32)
+        self.ctx = dict(cu_seqlens_q=torch.arange(batch + 1, dtype=torch.int32),
+                        cu_seqlens_k=torch.tensor([0] + list(np.cumsum(self.lens)),
+                                                  dtype=torch.int32),
                         slot_mapping=slots, block_tables=bt, is_prefill=False)
-        self.ids = torch.randint(0, 10000, (n_seqs,), generator=g)
-        self.cos_sin = L.rope_cos_sin(self.one.max_pos, self.one.head_dim, self.one.theta)
-        h = self.layer()
-        a = time.perf_counter()
-        OM.compute_logits(self.one, self.W, h, self.ctx)
-        self.t_head = time.perf_counter() - a
+        self.ids = torch.randint(0, 10000, (batch,), generator=g)
+        self.cos_sin = L.rope_cos_sin(self.shape.max_pos, self.shape.head_dim, self.shape.theta)
 
-    def layer(self):
-        return self.OM.forward(self.one, self.W, self.ids, self.pos, self.ctx, self.kv,
-                               cos_sin=self.cos_sin)
-
-    def time_layer(self) -> float:
+    def step(self) -> float:
+        """One decode step (seconds); feeds its tokens back as the next ids."""
         a = time.perf_counter()
-        self.layer()
+        h = self.OM.forward(self.shape, self.W, self.ids, self.pos, self.ctx, self.kv,
+                            cos_sin=self.cos_sin)
+        logits = self.OM.compute_logits(self.shape, self.W, h, self.ctx)
+        self.ids = logits.argmax(-1)
         return time.perf_counter() - a
 
-    def tok_per_s(self, t_layer: float) -> float:
-        return self.n / (t_layer * self.full.layers + self.t_head)
-
-    def describe(self, reps: int) -> dict:
+    def describe(self, steps: int) -> dict:
         return {"unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                "sample": (f"oracle torch-CPU port (bf16 F.linear as the reference): {reps} x one "
-                           f"Qwen3-8B decoder layer over {self.n} decode sequences of the mix "
-                           f"(mean ctx {np.mean(self.lens):.0f}) + LM head; tok/s extrapolated "
-                           f"to 36 layers")}
+                "sample": (f"oracle torch-CPU port of the reference path (bf16 F.linear as the "
+                           f"reference): {steps} full decode step(s) of the {self.n}-sequence mix "
+                           f"(mean ctx {np.mean(self.lens):.0f}) through 36 Qwen3-8B layers, LM head "
+                           f"over 151936 tokens and argmax; the 36 layers share one layer's "
+                           f"random weights and K/V pages")}
 
 
 def cpu_baseline(seconds: float, seed: int) -> dict:
-    smp = CpuDecodeSample(n_seqs=8, seed=seed)
+    """Full decode steps of the bench's workload on the host cores, as many
+    as fit `seconds` (at least one)."""
+    smp = CpuDecodeStep(seed=seed)
     times = []
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < seconds or not times:
-        times.append(smp.time_layer())
+    while not times or time.perf_counter() - t0 + times[-1] < seconds:
+        times.append(smp.step())
     d = smp.describe(len(times))
-    d["value"] = smp.tok_per_s(float(np.median(times)))
+    d["value"] = smp.n / float(np.mean(times))
     return d
 
 
 def run_reference_arm(args, rank: int, world: int):
+    """The reference arm: the CPU port on the host cores, full decode steps of
+    the same 256-sequence workload.  A CPU step takes tens of seconds, so the
+    run does at most `--cpu-max-steps` timed steps after one warm-up step and
+    reports the counts it actually ran."""
     if rank != 0:
         return
-    smp = CpuDecodeSample(n_seqs=8, seed=args.seed)
-    for _ in range(args.warmup):
-        smp.time_layer()
-    times = [smp.time_layer() for _ in range(args.steps)]
-    value = smp.tok_per_s(float(np.mean(times)))
-    d = smp.describe(len(times))
+    smp = CpuDecodeStep(seed=args.seed, batch=args.batch)
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        smp.step()
+    steps = max(1, min(args.steps, args.cpu_max_steps))
+    times = [smp.step() for _ in range(steps)]
+    ms = 1000.0 * float(np.mean(times))
+    value = smp.n / (ms / 1000.0)
+    d = smp.describe(steps)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * 256 / value, "higher_is_better": True, "scaling": "strong",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+        "steps_requested": args.steps, "warmup_requested": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": 256, "tp": 1, "device": "host CPU"},
+        "config": {"workload": WORKLOAD, "batch": smp.n, "tp": 1, "parallelism": "tp1",
+                   "mean_ctx": float(np.mean(smp.lens)), "block_size": BLOCK,
+                   "device": "host CPU"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": d["cores"], "kind": "port",
                          "sample": d["sample"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -674,7 +707,10 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--cpu-seconds", type=float, default=25.0,
+                    help="CPU baseline sample length (whole decode steps, at least one)")
+    ap.add_argument("--cpu-max-steps", type=int, default=3,
+                    help="reference arm: timed CPU steps at most (each takes tens of seconds)")
     ap.add_argument("--no-fused-ar", dest="fused_ar", action="store_false")
     ap.add_argument("--ar-mode", default="auto", choices=["auto", "oneshot", "twoshot"],
                     help="fused all-reduce exchange (allreduce workload)")

@@ -129,6 +129,17 @@ int b200_linear_allreduce(const void* x, long long ldx, const void* w, long long
                           void* const* done, long long stage_rows, long long ldo,
                           long long max_positions, int one_shot, b200_stream_t stream);
 
+/* Whether b200_linear_allreduce would launch (T, N, K) at `world` ranks with
+ * these buffer sizes (*supported = 1) or refuse it with B200_ERR_UNSUPPORTED
+ * (*supported = 0; b200_last_error() gives the reason).  Launches nothing.
+ * The answer depends only on the shapes, the sizes and the device type, so
+ * ranks of one job on identical GPUs agree; callers still agree on it with a
+ * collective before choosing between the fused path and
+ * b200_linear + torch.distributed.all_reduce (src/layers/linear.py:169-173),
+ * so that no rank takes the other path. */
+int b200_linear_allreduce_supported(int T, int N, int K, int world, long long stage_rows,
+                                    long long ldo, long long max_positions, int* supported);
+
 /* CUDA IPC helpers for the symmetric buffers: export the allocation that
  * holds `ptr` (64-byte handle + offset of ptr inside it), map a peer's
  * export into this process, and unmap it. */

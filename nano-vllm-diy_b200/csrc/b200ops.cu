@@ -334,6 +334,13 @@ bool csk_forced() {
   return e && *e == '3';
 }
 
+// Decode attention's PV operand: bf16 hi + lo parts of P (default) or
+// B200_DECODE_P=bf16 for the hi part alone (flash attention's rounding).
+int decode_p_lo() {
+  const char* e = getenv("B200_DECODE_P");
+  return (e && std::strcmp(e, "bf16") == 0) ? 0 : 1;
+}
+
 bool grouped_allowed() {
   const char* e = getenv("B200_GEMM_SCHED");
   return !(e && std::strcmp(e, "streamk") == 0);
@@ -651,29 +658,14 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
   return check_launch("gemm_tn_tcgen05_kernel");
 }
 
-// Fused RowParallelLinear: GEMM + all-reduce in one launch (EPI_ALLREDUCE).
-int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
-                       int T, int N, int K, const AllReducePeers& ar, long long max_positions,
-                       cudaStream_t st) {
-  if (T <= 0) return B200_OK;
-  if (N <= 0 || K <= 0 || N % 8) return fail(B200_ERR_INVALID, "linear_allreduce: N=%d must be a multiple of 8", N);
-  if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K)
-    return fail(B200_ERR_INVALID, "linear_allreduce: K and row strides must be multiples of 8");
-  if (!aligned16(x) || !aligned16(w)) return fail(B200_ERR_INVALID, "linear_allreduce: x and w must be 16-byte aligned");
-  if (ar.world < 1 || ar.world > kMaxTpRanks || ar.rank < 0 || ar.rank >= ar.world)
-    return fail(B200_ERR_INVALID, "linear_allreduce: rank %d / world %d", ar.rank, ar.world);
-  if (T > ar.stage_rows || ar.ldo < N || ar.ldo % 8)
-    return fail(B200_ERR_UNSUPPORTED, "linear_allreduce: %d rows exceed the %lld staged rows (or ldo)", T, ar.stage_rows);
-  for (int r = 0; r < ar.world; ++r)
-    if (!ar.stage[r] || !ar.out[r] || !ar.flags[r] || !ar.done[r] || !aligned16(ar.stage[r]) ||
-        !aligned16(ar.out[r]))
-      return fail(B200_ERR_PEER, "linear_allreduce: peer buffers of rank %d are missing", r);
-  DeviceState* ds;
-  if (int r = device_state(&ds)) return r;
+// Plan of the fused RowParallelLinear launch: the single-SM GEMM plan with
+// the largest K split (down to none) whose grid is co-resident, since owners
+// wait for their peers' CTAs.  B200_ERR_UNSUPPORTED when no grid fits or the
+// CTA positions exceed the flags.  Depends only on (T, N, K), the device type
+// and `max_positions`, so every rank of a job gets the same answer.
+int plan_allreduce(DeviceState* ds, int T, int N, int K, long long max_positions, GemmPlan* out) {
   GemmPlan p = plan_gemm(ds, T, N, K, false);
   if (int r = ensure_smem(ds, 1u, gemm_tn_tcgen05_kernel, p.smem)) return r;
-  // every CTA must be resident at once (owners wait for peers' CTAs): take the
-  // largest K split, down to none, whose grid fits the co-resident slots
   // co-resident CTAs for a split (occupancy queries are slow: cached per
   // device, split and shared-memory size)
   static long long resident_cache[kMaxDevices][9][4] = {};
@@ -733,6 +725,31 @@ int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ld
   const long long resident = resident_for(p.splits);
   if (ctas > resident)
     return fail(B200_ERR_UNSUPPORTED, "linear_allreduce: %lld CTAs cannot all be resident (%lld)", ctas, resident);
+  *out = p;
+  return B200_OK;
+}
+
+// Fused RowParallelLinear: GEMM + all-reduce in one launch (EPI_ALLREDUCE).
+int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ldw, const void* bias,
+                       int T, int N, int K, const AllReducePeers& ar, long long max_positions,
+                       cudaStream_t st) {
+  if (T <= 0) return B200_OK;
+  if (N <= 0 || K <= 0 || N % 8) return fail(B200_ERR_INVALID, "linear_allreduce: N=%d must be a multiple of 8", N);
+  if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K)
+    return fail(B200_ERR_INVALID, "linear_allreduce: K and row strides must be multiples of 8");
+  if (!aligned16(x) || !aligned16(w)) return fail(B200_ERR_INVALID, "linear_allreduce: x and w must be 16-byte aligned");
+  if (ar.world < 1 || ar.world > kMaxTpRanks || ar.rank < 0 || ar.rank >= ar.world)
+    return fail(B200_ERR_INVALID, "linear_allreduce: rank %d / world %d", ar.rank, ar.world);
+  if (T > ar.stage_rows || ar.ldo < N || ar.ldo % 8)
+    return fail(B200_ERR_UNSUPPORTED, "linear_allreduce: %d rows exceed the %lld staged rows (or ldo)", T, ar.stage_rows);
+  for (int r = 0; r < ar.world; ++r)
+    if (!ar.stage[r] || !ar.out[r] || !ar.flags[r] || !ar.done[r] || !aligned16(ar.stage[r]) ||
+        !aligned16(ar.out[r]))
+      return fail(B200_ERR_PEER, "linear_allreduce: peer buffers of rank %d are missing", r);
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  GemmPlan p{};
+  if (int r = plan_allreduce(ds, T, N, K, max_positions, &p)) return r;
   CUtensorMap tmW, tmX;
   if (int r = make_tmap(&tmW, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kGemmBK, (uint32_t)kGemmBM)) return r;
   if (int r = make_tmap(&tmX, x, (uint64_t)K, (uint64_t)T, (uint64_t)ldx, kGemmBK, (uint32_t)p.BN)) return r;
@@ -1053,6 +1070,7 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
     a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
     a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
     a.err = ds->err;
+    a.p_lo = decode_p_lo();
     const int smem = dec_smem_bytes();
     if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
     if (int r = launch_decode(ds, tmK, tmV, tmQ, a, smem, st)) return r;
@@ -1108,6 +1126,26 @@ int b200_ipc_close(void* ptr, unsigned long long offset) {
   if (!ptr) return B200_OK;
   const cudaError_t e = cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset);
   if (e != cudaSuccess) return fail(B200_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return B200_OK;
+}
+
+int b200_linear_allreduce_supported(int T, int N, int K, int world, long long stage_rows,
+                                    long long ldo, long long max_positions, int* supported) {
+  if (!supported) return fail(B200_ERR_INVALID, "linear_allreduce_supported: null result");
+  *supported = 0;
+  if (T <= 0 || N <= 0 || K <= 0 || N % 8 || K % 8 || world < 1 || world > kMaxTpRanks)
+    return fail(B200_ERR_INVALID, "linear_allreduce_supported: T=%d N=%d K=%d world=%d", T, N, K, world);
+  if (T > stage_rows || ldo < N || ldo % 8) {
+    fail(B200_ERR_UNSUPPORTED, "linear_allreduce: %d rows exceed the %lld staged rows (or ldo)", T, stage_rows);
+    return B200_OK;
+  }
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  GemmPlan p{};
+  const int r = plan_allreduce(ds, T, N, K, max_positions, &p);
+  if (r == B200_ERR_UNSUPPORTED) return B200_OK;  // *supported stays 0; the reason is the last error
+  if (r) return r;
+  *supported = 1;
   return B200_OK;
 }
 
@@ -1233,6 +1271,7 @@ extern "C" int b200_paged_decode_attention_static(
   a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
   a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
   a.err = ds->err;
+  a.p_lo = decode_p_lo();
   const int smem = dec_smem_bytes();
   if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
   if (int r = launch_decode(ds, tmK, tmV, tmQ, a, smem, st)) return r;

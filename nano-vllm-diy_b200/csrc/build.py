@@ -15,7 +15,8 @@ REPO = os.path.dirname(PKG)
 LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libb200ops.so")
 SOURCES = ["b200ops.cu"]
-HEADERS = ["common.cuh", "gemm.cuh", "attention.cuh", "decode_attention.cuh", "elementwise.cuh"]
+HEADERS = ["common.cuh", "gemm.cuh", "gemm_pair.cuh", "attention.cuh", "decode_attention.cuh",
+           "elementwise.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 

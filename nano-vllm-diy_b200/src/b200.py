@@ -45,6 +45,7 @@ _SIGNATURES = {
     "b200_linear_allreduce": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _i, _i, _i, _i, _i,
                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _ll, _ll, _ll, _i,
                                _c_void_p], _i),
+    "b200_linear_allreduce_supported": ([_i, _i, _i, _i, _ll, _ll, _ll, ctypes.POINTER(_i)], _i),
     "b200_ipc_export": ([_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_ulonglong)], _i),
     "b200_ipc_import": ([_c_void_p, ctypes.c_ulonglong, ctypes.POINTER(_c_void_p)], _i),
     "b200_ipc_close": ([_c_void_p, ctypes.c_ulonglong], _i),
@@ -163,9 +164,26 @@ def launch_count() -> int:
     return int(load_library().b200_launch_count())
 
 
+# device error bits (include/b200ops.h): a bounded wait ran out
+_TIMEOUT_BITS = 0x1 | 0x2
+# the GEMM workspace starts with 4 KiB of split-K flags and counters
+_GEMM_FLAG_BYTES = 4096
+
+
 def device_error(clear: bool = True) -> int:
+    """The device error word (synchronises the device).  With `clear`, it is
+    reset; if a bounded wait ran out, the counters at the head of this
+    device's attention and GEMM workspaces are zeroed too: a kernel that gave
+    up waiting can leave counts that the next call would trust."""
     v = ctypes.c_uint(0)
     _check(load_library().b200_device_error(ctypes.byref(v), int(clear)), "b200_device_error")
+    if clear and v.value & _TIMEOUT_BITS:
+        dev = torch.cuda.current_device()
+        heads = {"attn": attention_workspace_bytes(0, 0, 1), "gemm": _GEMM_FLAG_BYTES}
+        for (d, kind), buf in _workspaces.items():
+            if d == dev and kind in heads:
+                buf[:heads[kind]].zero_()
+        torch.cuda.synchronize()
     return v.value
 
 
@@ -264,6 +282,16 @@ def ipc_close(ptr: int, offset: int) -> None:
     _check(load_library().b200_ipc_close(ctypes.c_void_p(ptr), offset), "b200_ipc_close")
 
 
+def linear_allreduce_supported(T: int, N: int, K: int, world: int, stage_rows: int, ldo: int,
+                               max_positions: int) -> bool:
+    """Whether the fused GEMM + all-reduce would launch this shape (no launch)."""
+    ok = ctypes.c_int(0)
+    _check(load_library().b200_linear_allreduce_supported(T, N, K, world, stage_rows, ldo,
+                                                          max_positions, ctypes.byref(ok)),
+           "b200_linear_allreduce_supported")
+    return bool(ok.value)
+
+
 def linear_allreduce(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, rank: int,
                      world: int, stage: list[int], out: list[int], flags: list[int],
                      done: list[int], stage_rows: int, ldo: int, max_positions: int,
@@ -304,6 +332,18 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
     except ValueError:
         x = x.contiguous()
         rows, xs = _rows(x)
+    # the kernel indexes out, residual and residual_out as contiguous rows of
+    # `dim` elements: anything else would be read or written out of bounds
+    if weight.shape != (dim,):
+        raise ValueError(f"rms_norm: weight {tuple(weight.shape)} for rows of {dim}")
+    for name, t in (("out", out), ("residual", residual), ("residual_out", residual_out)):
+        if t is not None and t.shape != x.shape:
+            raise ValueError(f"rms_norm: {name} has shape {tuple(t.shape)}, x has {tuple(x.shape)}")
+    for name, t in (("out", out), ("residual_out", residual_out)):
+        if t is not None and not t.is_contiguous():
+            raise ValueError(f"rms_norm: {name} must be contiguous")
+    _cuda(out, residual_out)
+    _bf16(out, residual_out)
     if out is None:
         out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     if residual is not None:

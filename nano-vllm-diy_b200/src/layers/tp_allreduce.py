@@ -26,9 +26,16 @@ rank's address of each part.
 The returned tensor is a view of an output buffer that the call after the
 next one overwrites (two buffers alternate), which is how the decoder
 consumes it (the next RMSNorm reads it before the next row-parallel layer).
-Batches that the fused kernel does not take (more than max_tokens rows, or
-a launch whose CTAs could not all be resident) fall back to GEMM +
-torch.distributed.all_reduce on every rank alike.
+
+Which path a call takes is decided the same way on every rank, so that no
+rank waits in NCCL while its peers wait on fused-kernel flags:
+  * shape conditions known on every rank (more than max_tokens rows, N
+    wider than the staged rows) pick GEMM + torch.distributed.all_reduce;
+  * the launchability of a shape (every CTA co-resident, flag positions) is
+    asked of the library once per (T, N, K) outside graph capture, and the
+    ranks agree on the answer with an all_reduce(MIN) before any of them
+    uses it;
+  * a fused launch that then fails raises instead of switching paths.
 """
 from __future__ import annotations
 
@@ -84,6 +91,7 @@ class FusedRowParallel:
         self.fused_calls = 0
         self.fallback_calls = 0
         self.fallback_reason = ""
+        self._plans: dict[tuple[int, int, int], bool] = {}
         dist.barrier(group=group)
 
     @classmethod
@@ -93,22 +101,44 @@ class FusedRowParallel:
     def _addrs(self, off: int) -> list[int]:
         return [b + off for b in self.bases]
 
+    def fused_ok(self, T: int, N: int, K: int) -> bool:
+        """Whether (T, N, K) runs fused -- the same answer on every rank.  The
+        first query of a shape is a collective (outside graph capture)."""
+        if T > self.max_tokens or N > self.ldo:
+            return False
+        key = (T, N, K)
+        ok = self._plans.get(key)
+        if ok is None:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(f"fused all-reduce: shape {key} first seen inside a CUDA-graph "
+                                   "capture; run the batch size eagerly first (warm-up)")
+            local = b200.linear_allreduce_supported(T, N, K, self.world, self.max_tokens, self.ldo,
+                                                    MAX_POSITIONS)
+            flag = torch.tensor([1 if local else 0], dtype=torch.int32, device=self.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+            ok = self._plans[key] = bool(flag.item())
+            if not ok:
+                self.fallback_reason = (b200.load_library().b200_last_error().decode(errors="replace")
+                                        if not local else f"a peer cannot launch {key} fused")
+        return ok
+
     def linear_allreduce(self, x: torch.Tensor, w: torch.Tensor,
                          bias: torch.Tensor | None = None) -> torch.Tensor:
         T = x.reshape(-1, x.shape[-1]).shape[0]
-        N = w.shape[0]
-        if T <= self.max_tokens and N <= self.ldo:
+        N, K = w.shape[0], w.shape[1]
+        if self.fused_ok(T, N, K):
             idx = self._flip
             rc = b200.linear_allreduce(
                 x, w, bias, self.rank, self.world, self._addrs(self.off_stage),
                 self._addrs(self.off_out[idx]), self._addrs(self.off_flags),
                 self._addrs(self.off_done), self.max_tokens, self.ldo, MAX_POSITIONS, self.one_shot)
-            if rc == 0:
-                self._flip ^= 1
-                self.fused_calls += 1
-                return self.outs[idx][:T, :N].view(*x.shape[:-1], N)
+            if rc != 0:
+                msg = b200.load_library().b200_last_error().decode(errors="replace")
+                raise RuntimeError(f"fused GEMM + all-reduce refused a planned launch: {msg}")
+            self._flip ^= 1
+            self.fused_calls += 1
+            return self.outs[idx][:T, :N].view(*x.shape[:-1], N)
         self.fallback_calls += 1
-        self.fallback_reason = b200.load_library().b200_last_error().decode(errors="replace")
         y = b200.linear(x, w, bias)
         dist.all_reduce(y, group=self.group)
         return y

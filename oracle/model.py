@@ -53,8 +53,12 @@ def forward(shape: Qwen3Shape, W: dict, input_ids: torch.Tensor, positions: torc
         else:
             x, residual = L.rms_norm_residual(h, residual, W[p + "input_layernorm.weight"], eps)
         # Qwen3Attention.forward (qwen3.py:74-91)
-        wqkv = torch.cat([W[p + "self_attn.q_proj.weight"], W[p + "self_attn.k_proj.weight"],
-                          W[p + "self_attn.v_proj.weight"]], 0)
+        # the reference's QKVParallelLinear holds the three projections stacked
+        # [q | k | v] (linear.py:130-141); a caller may pass them pre-stacked
+        wqkv = W.get(p + "self_attn.qkv_proj.weight")
+        if wqkv is None:
+            wqkv = torch.cat([W[p + "self_attn.q_proj.weight"], W[p + "self_attn.k_proj.weight"],
+                              W[p + "self_attn.v_proj.weight"]], 0)
         qkv = L.linear(x, wqkv)
         q, k, v = qkv.split([Hq * d, Hkv * d, Hkv * d], dim=-1)
         q = q.reshape(-1, Hq, d)
@@ -74,7 +78,9 @@ def forward(shape: Qwen3Shape, W: dict, input_ids: torch.Tensor, positions: torc
         h = _row_parallel(o.reshape(-1, Hq * d), W[p + "self_attn.o_proj.weight"], tp)
         x, residual = L.rms_norm_residual(h, residual, W[p + "post_attention_layernorm.weight"], eps)
         # Qwen3MLP.forward (qwen3.py:119-123)
-        wgu = torch.cat([W[p + "mlp.gate_proj.weight"], W[p + "mlp.up_proj.weight"]], 0)
+        wgu = W.get(p + "mlp.gate_up_proj.weight")  # [gate | up] (linear.py:98-102)
+        if wgu is None:
+            wgu = torch.cat([W[p + "mlp.gate_proj.weight"], W[p + "mlp.up_proj.weight"]], 0)
         if tp == 1:
             act = L.silu_and_mul(L.linear(x, wgu))
         else:

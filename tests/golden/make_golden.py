@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
-Run in a container where the reference checkout is available (path given by
-REF_DIR, default the read-only mount this build used); the outputs are small
+Run in a container where the reference checkout is available, with its path
+in the REF_DIR environment variable (required); the outputs are small
 .pt files next to this script and are committed.  Nothing on a GPU machine
 reads the reference: the tests only load these files.
 
@@ -33,7 +33,7 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_DIR = os.environ.get("REF_DIR", "/root/reference")
+REF_DIR = os.environ.get("REF_DIR", "")
 
 import torch  # noqa: E402
 import torch.nn.functional as F  # noqa: E402
@@ -355,6 +355,8 @@ def make_tiny_model(A):
 
 
 def main():
+    if not REF_DIR or not os.path.isdir(os.path.join(REF_DIR, "src")):
+        raise SystemExit("set REF_DIR to the reference checkout (the directory holding src/)")
     A = import_reference()
     torch.manual_seed(0)
     torch.save(make_layers(), os.path.join(HERE, "layers.pt"))

@@ -1,8 +1,9 @@
 """bench.py's reference arm (the CPU port of the reference path) prints the
 one-line JSON contract the driver reads: the same metric, unit and workload
 as the B200 arm, plus `impl`, `cpu_baseline` and an `e2e` object with no
-host-device traffic.  CPU only (about 15 s: one decoder layer of the
-Qwen3-8B shape over 8 sequences)."""
+host-device traffic.  CPU only: run here on 8 sequences of the mix (the
+default is the full 256), one warm-up and one timed full decode step through
+the 36 Qwen3-8B layers and the LM head (about a minute)."""
 import json
 import os
 import subprocess
@@ -12,7 +13,8 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def test_reference_arm_prints_the_contract_line():
-    proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3"],
+    proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "3",
+                           "--batch", "8"],
                           cwd=REPO, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stderr[-2000:]
     line = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")][-1]
@@ -20,9 +22,12 @@ def test_reference_arm_prints_the_contract_line():
     assert d["impl"] == "reference"
     assert d["metric"].startswith("decode tok/s") and d["unit"] == "tok/s"
     assert d["value"] > 0 and d["ms_per_step"] > 0
-    assert d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 3
+    # the CPU arm runs at most one warm-up step and reports what it ran
+    assert d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 1
+    assert d["steps_requested"] == 1 and d["warmup_requested"] == 3
     assert d["higher_is_better"] is True and d["dtype"] == "bf16"
     assert d["config"]["workload"] == "qwen3-8b-decode-mix256"
+    assert d["config"]["batch"] == 8
     cb = d["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == d["value"]
     assert cb["unit"] == "tok/s" and cb["sample"]

@@ -4,13 +4,10 @@ restatement of the reference forward, on the same seeded random-init weights.
 Bars (from the task statement): layer / logit outputs within max rel err
 2e-2 of the fp32-accumulated oracle; KV-cache slot writes bit-exact in
 position (only slots named by slot_mapping change); greedy tokens agree on
->= 99% of the first 64 decode steps.  Greedy agreement is measured with
-teacher forcing (both sides see the oracle's token history), so that one
-near-tie does not fork the two sequences.  The >= 99% bar is applied to the
-steps whose oracle top-2 logits are more than one bf16 ulp apart (on the
-others the two bf16 logits are tied or adjacent and either pick is the
-reference's own rounding noise); the raw rate over all steps must stay
->= 95%.
+>= 99% of the first 64 decode steps, over all steps of 16 sequences.
+Greedy agreement is measured with teacher forcing (both sides see the
+oracle's token history), so that one near-tie does not fork the two
+sequences; every disagreement is printed with the oracle's top-2 margin.
 """
 import pytest
 import torch
@@ -158,20 +155,36 @@ def test_cuda_graph_decode_matches_eager():
     runner.release_graphs()
 
 
+def _fp32_linear_weights(W: dict, tie: bool) -> dict:
+    """The oracle's linear() computes in fp32 from bf16 weights; handing it
+    the same values already widened to fp32 gives identical results without
+    re-widening 0.6 G parameters at every step."""
+    out = dict(W)
+    for k, v in W.items():
+        if k.endswith("proj.weight") or k == "lm_head.weight":
+            out[k] = v.float()
+    if tie:
+        out["lm_head.weight"] = W["model.embed_tokens.weight"].float()
+    return out
+
+
 def test_greedy_agreement_64_steps():
-    """Qwen3-0.6B architecture (28 layers, tied embeddings), 4 sequences,
-    64 teacher-forced greedy decode steps through CUDA graphs."""
+    """Qwen3-0.6B architecture (28 layers, tied embeddings, vocab 151936), 16
+    sequences, 64 teacher-forced greedy decode steps through CUDA graphs: the
+    argmax token must agree with the oracle's on >= 99% of the 1024 steps."""
     from src.layers.pos_embedding import _table_cpu
     from oracle.weights import QWEN3_0_6B
     import dataclasses
     shape = dataclasses.replace(QWEN3_0_6B, max_pos=4096)
     W = random_weights(shape, seed=11)
     g = torch.Generator().manual_seed(12)
+    nseq = 16
     prompts = [torch.randint(0, 10000, (int(n),), generator=g).tolist()
-               for n in torch.randint(20, 120, (4,), generator=g)]
-    runner = _runner(shape, W, num_blocks=8, max_num_seqs=4)
-    runner.capture_cudagraph([4])
-    okv = OM.OracleKV(shape, 8, PAGE)
+               for n in torch.randint(20, 120, (nseq,), generator=g)]
+    runner = _runner(shape, W, num_blocks=2 * nseq, max_num_seqs=nseq)
+    runner.capture_cudagraph([nseq])
+    W = _fp32_linear_weights(W, shape.tie)
+    okv = OM.OracleKV(shape, 2 * nseq, PAGE)
     cos_sin = _table_cpu(shape.max_pos, shape.head_dim, float(shape.theta))
     seqs = _seqs(prompts, 2)
     meta = prepare_seqs(seqs, PAGE)
@@ -179,7 +192,7 @@ def test_greedy_agreement_64_steps():
     rl = OM.compute_logits(shape, W, rh, _octx(meta))
     gpu_tok = runner.step_greedy(seqs)
     agree = total = 0
-    dec_agree = dec_total = 0
+    misses = []
     for step in range(65):  # the prefill token, then 64 decode steps
         ref_tok = rl.float().argmax(-1).tolist()
         if step > 0:
@@ -187,14 +200,13 @@ def test_greedy_agreement_64_steps():
             total += len(ref_tok)
             top2 = rl.float().topk(2, -1).values
             for i, (a, b) in enumerate(zip(gpu_tok, ref_tok)):
-                margin = (top2[i, 0] - top2[i, 1]).item()
-                # one bf16 ulp at the magnitude of the top logit
-                ulp = 2.0 ** (torch.frexp(top2[i, 0].abs()).exponent.item() - 8)
-                if margin > ulp:
-                    dec_total += 1
-                    dec_agree += int(a == b)
                 if a != b:
-                    print(f"step {step} seq {i}: gpu {a} oracle {b} oracle top-2 margin {margin:.4f} (ulp {ulp})")
+                    margin = (top2[i, 0] - top2[i, 1]).item()
+                    # one bf16 ulp at the magnitude of the top logit
+                    ulp = 2.0 ** (torch.frexp(top2[i, 0].abs()).exponent.item() - 8)
+                    misses.append((step, i, a, b, margin, ulp))
+                    print(f"step {step} seq {i}: gpu {a} oracle {b}; oracle top-2 margin "
+                          f"{margin:.5f} (one bf16 ulp: {ulp})")
         if step == 64:
             break
         for s, t in zip(seqs, ref_tok):
@@ -206,10 +218,7 @@ def test_greedy_agreement_64_steps():
         rl = OM.compute_logits(shape, W, rh, _octx(meta))
         gpu_tok = runner.step_greedy(seqs)
     rate = agree / total
-    dec_rate = dec_agree / max(dec_total, 1)
-    print(f"greedy agreement {agree}/{total} = {rate:.4f}; on steps whose oracle top-2 logits "
-          f"differ by more than one bf16 ulp: {dec_agree}/{dec_total} = {dec_rate:.4f}")
-    # bf16 logits tie or sit one ulp apart on a few percent of random-init
-    # steps; there the reference's own choice is decided by rounding noise.
-    assert dec_rate >= 0.99, dec_rate
-    assert rate >= 0.95, rate
+    print(f"greedy agreement {agree}/{total} = {rate:.4f}")
+    runner.release_graphs()
+    assert total == 64 * nseq
+    assert rate >= 0.99, (rate, misses)

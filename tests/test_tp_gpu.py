@@ -1,13 +1,16 @@
-"""Tensor parallelism on 2 GPUs (NCCL process group, one process per GPU).
+"""Tensor parallelism on 2, 4 and 8 GPUs (NCCL process group, one process
+per GPU; each case is skipped when the machine shows fewer GPUs).
 
-* the fused RowParallelLinear (GEMM + all-reduce over NVLink peer memory)
-  against the oracle's restatement of src/layers/linear.py:169-173 --
-  sum over ranks of each rank's bf16 partial product, rounded once;
-  every rank must hold the bit-identical result;
+* the fused RowParallelLinear (GEMM + all-reduce over NVLink peer memory),
+  both exchange patterns, against the oracle's restatement of
+  src/layers/linear.py:169-173 -- sum over ranks of each rank's bf16 partial
+  product, rounded once; every rank must hold the bit-identical result;
 * fifty calls in a row (the handshake flags reset themselves);
-* the Qwen3 model at tp = 2 against the oracle's tp = 2 forward.
-
-Skipped unless the machine shows at least two GPUs.
+* BASELINE config 1 (x [512, 1536], W [1024, 1536] per rank, world 2, seed
+  0) on the fused kernel against the golden rows of the reference's own
+  RowParallelLinear under gloo;
+* the Qwen3 model at tp = world against the oracle's tp = world forward,
+  prefill and CUDA-graph decode steps.
 """
 import os
 import socket
@@ -79,6 +82,43 @@ def _fused_worker(rank, world, port, one_shot):
         dist.destroy_process_group()
 
 
+def _config1_worker(rank, world, port, one_shot):
+    """BASELINE config 1 on the fused kernel: the reference's RowParallelLinear
+    (F.linear per rank + all_reduce) gave the golden rows under gloo."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "nano-vllm-diy_b200")]
+    import torch.distributed as dist
+    from oracle import layers as L
+    from oracle import model as OM
+    from src import b200
+    from src.layers.tp_allreduce import FusedRowParallel
+    dev = _init(rank, world, port)
+    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=1024, one_shot=one_shot)
+    try:
+        golden = torch.load(os.path.join(here, "golden", "row_parallel_c1.pt"))
+        gen = torch.Generator().manual_seed(0)
+        x = torch.randn(512, 3072, generator=gen).to(torch.bfloat16)
+        w = (torch.randn(1024, 3072, generator=gen) * 0.02).to(torch.bfloat16)
+        xs, ws = x.chunk(world, -1), w.chunk(world, 1)
+        y = comm.linear_allreduce(xs[rank].contiguous().to(dev), ws[rank].contiguous().to(dev))
+        torch.cuda.synchronize()
+        assert comm.fallback_calls == 0, comm.fallback_reason
+        yc = y.cpu()
+        assert L.rel_err(yc[::64], golden["rows"]) <= 1e-2
+        assert L.rel_err(yc, OM._row_parallel(x, w, world)) <= 1e-2
+        ref32 = x.float() @ w.float().t()
+        assert L.rel_err(yc, ref32) <= 1e-2
+        parts = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(parts, y.contiguous())
+        for p in parts:
+            assert torch.equal(p, parts[0]), "ranks disagree"
+        assert b200.device_error(clear=True) == 0
+    finally:
+        comm.close()
+        dist.destroy_process_group()
+
+
 def _model_worker(rank, world, port):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -94,10 +134,11 @@ def _model_worker(rank, world, port):
     from src.layers.pos_embedding import _table_cpu
     from src.layers.tp_allreduce import FusedRowParallel
     dev = _init(rank, world, port)
-    tp_comm.set_comm(FusedRowParallel(dev, max_tokens=512, max_hidden=512))
+    # 8 kv heads and 16 q heads: one kv head per rank at tp 8
+    shape = Qwen3Shape(hidden=1024, layers=2, heads=16, kv_heads=8, head_dim=128, inter=2048,
+                       vocab=4096, max_pos=4096)
+    tp_comm.set_comm(FusedRowParallel(dev, max_tokens=512, max_hidden=shape.hidden))
     try:
-        shape = Qwen3Shape(hidden=512, layers=2, heads=4, kv_heads=2, head_dim=128, inter=1024,
-                           vocab=4096, max_pos=4096)
         W = random_weights(shape, seed=21)
         runner = ModelRunner(shape.hf_config(), rank=rank, world_size=world, max_num_seqs=8,
                              max_seq_len=4096, device=dev)
@@ -134,18 +175,28 @@ def _model_worker(rank, world, port):
         dist.destroy_process_group()
 
 
-@pytest.fixture
-def two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _need(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("one_shot", [True, False], ids=["one-shot", "two-shot"])
+def test_fused_row_parallel_allreduce(world, one_shot):
+    _need(world)
+    import torch.multiprocessing as mp
+    mp.spawn(_fused_worker, args=(world, _free_port(), one_shot), nprocs=world, join=True)
 
 
 @pytest.mark.parametrize("one_shot", [True, False], ids=["one-shot", "two-shot"])
-def test_fused_row_parallel_allreduce(two_gpus, one_shot):
+def test_fused_allreduce_config1_matches_reference_golden(one_shot):
+    _need(2)
     import torch.multiprocessing as mp
-    mp.spawn(_fused_worker, args=(2, _free_port(), one_shot), nprocs=2, join=True)
+    mp.spawn(_config1_worker, args=(2, _free_port(), one_shot), nprocs=2, join=True)
 
 
-def test_qwen3_tp2_matches_oracle(two_gpus):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_qwen3_tp_matches_oracle(world):
+    _need(world)
     import torch.multiprocessing as mp
-    mp.spawn(_model_worker, args=(2, _free_port()), nprocs=2, join=True)
+    mp.spawn(_model_worker, args=(world, _free_port()), nprocs=world, join=True)
