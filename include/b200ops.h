@@ -271,6 +271,47 @@ int b200_paged_decode_attention_static(const void* q, long long q_stride, int nu
 int b200_embedding(const long long* ids, const void* weight, void* out, int T, int H,
                    long long vocab_start, long long vocab_end, b200_stream_t stream);
 
+/* Vocabulary-parallel embedding whose all-reduce is done as a scatter over
+ * NVLink: replaces src/layers/llm_head.py:38-49 (masked F.embedding of this
+ * rank's shard + dist.all_reduce).  Every rank calls it with the same ids;
+ * rank `rank` writes the rows of the ids in [vocab_start, vocab_end) into
+ * out[dst] of every rank dst (rows [0, T), row stride ld_out elements), and
+ * rank 0 also writes the zero rows of ids outside [0, vocab_size).  The last
+ * CTA signals the peers through flags[*] and waits (bounded) until every
+ * rank's rows have arrived, so out[rank] is complete when the launch
+ * completes.  out / flags are arrays of `world` addresses (this rank's view
+ * of each rank's buffer, its own at index rank); flags[r] points at rank r's
+ * uint32 [2][8] flag words and `state` at this rank's own uint32 [4] words
+ * (call epochs and a CTA counter), all zero before the first call.  world 1:
+ * the plain masked lookup into out[0]. */
+int b200_embedding_exchange(const long long* ids, const void* weight, int T, int H,
+                            long long vocab_start, long long vocab_end, long long vocab_size,
+                            int rank, int world, void* const* out, long long ld_out,
+                            void* const* flags, void* state, b200_stream_t stream);
+
+/* Token selection on this rank's vocabulary shard: keys[r] = the packed
+ * (score, global index) of row r's best column, where score = logit (greedy,
+ * temperatures == NULL) or logit / T_r - ln(max(E, 1e-10)) with E ~ Exp(1)
+ * taken from `noise` ([rows][noise_stride] fp32) or, when noise == NULL,
+ * drawn by Philox-4x32-10 keyed by (seed, row, global column, offset).  The
+ * maximum of the keys over the shards selects the same token as
+ * src/layers/sampler.py:4-17 (softmax(logits / T) / E, argmax) over the
+ * gathered logits of src/layers/llm_head.py:65-68 (lowest index on ties),
+ * so no logits need to be gathered.  One CTA per row. */
+int b200_select_tokens_partial(const void* logits, long long stride, int rows, int V,
+                               long long vocab_start, const float* temperatures, const float* noise,
+                               long long noise_stride, unsigned long long seed,
+                               unsigned long long offset, long long* keys, b200_stream_t stream);
+
+/* tokens[r] = the token of the maximum of keys[r] over the `world` ranks:
+ * every rank pushes its keys into key_slots[*] (int64 [2][world][max_rows]
+ * per rank), one signal round through flags[*] (as for
+ * b200_embedding_exchange, the other word), bounded wait, maximum per row.
+ * rows <= 1024.  world 1: tokens straight from the keys. */
+int b200_select_tokens_exchange(const long long* keys, int rows, int rank, int world,
+                                void* const* key_slots, void* const* flags, void* state,
+                                long long max_rows, long long* tokens, b200_stream_t stream);
+
 /* out[r] = argmax(logits[r, :V]) (first maximum), int64.  Greedy selection
  * over the logits returned by src/layers/llm_head.py:60-69. */
 int b200_argmax(const void* logits, long long stride, int rows, int V, long long* out,

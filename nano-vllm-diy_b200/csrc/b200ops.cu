@@ -20,6 +20,7 @@
 #include "decode_attention.cuh"
 #include "common.cuh"
 #include "elementwise.cuh"
+#include "exchange.cuh"
 #include "gemm.cuh"
 #include "gemm_pair.cuh"
 #include "../../include/b200ops.h"
@@ -334,13 +335,6 @@ bool csk_forced() {
   return e && *e == '3';
 }
 
-// Decode attention's PV operand: bf16 hi + lo parts of P (default) or
-// B200_DECODE_P=bf16 for the hi part alone (flash attention's rounding).
-int decode_p_lo() {
-  const char* e = getenv("B200_DECODE_P");
-  return (e && std::strcmp(e, "bf16") == 0) ? 0 : 1;
-}
-
 bool grouped_allowed() {
   const char* e = getenv("B200_GEMM_SCHED");
   return !(e && std::strcmp(e, "streamk") == 0);
@@ -458,48 +452,66 @@ GemmPlan plan_pair(DeviceState* ds, int T, int N, int K, bool silu_tiles, int* r
   return p;
 }
 
-// Plan of the pair kernel's cluster split-K mode (plain GEMMs): clusters of 2
-// pairs, one tile each, K halves.  NP = the smallest multiple of 32 (<= 256)
-// whose tiles all fit the co-resident clusters of 4 CTAs (more tiles keep more
-// SMs busy; 256 and waves of clusters when none fits).  `splits` = pairs
-// launched (2 per tile), 0 when the mode does not apply; *resident tells
-// whether every cluster is co-resident.
+// Plan of the pair kernel's cluster split-K mode (plain GEMMs): clusters of C
+// pairs (2C CTAs, C = 2..4), one tile each, K split C ways.  Among the (C, NP)
+// whose clusters are all co-resident (NP a multiple of 32, <= 256, the ring
+// able to receive the other members' partials), pick the smallest modelled
+// time: per SM, the TMA ingest of its K share (128 token rows + NP/2 weight
+// rows per 64-wide K block, ~74 GB/s measured per SM) plus the partial chunks
+// it receives through distributed shared memory.  B200_GEMM_CSK="C,NP" forces
+// a configuration (tuning).  `splits` = pairs launched (C per tile), 0 when
+// the mode does not apply; *resident tells whether every cluster is resident.
 GemmPlan plan_pair_cluster(DeviceState* ds, int T, int N, int K, bool* resident, int* rc) {
   GemmPlan best{};
+  double best_cost = 1e300;
   *rc = 0;
   *resident = false;
   const int num_kb = (K + kGemmBK - 1) / kGemmBK;
   if (num_kb < 2) return best;
+  int f_c = 0, f_np = 0;
+  const char* fe = getenv("B200_GEMM_CSK");
+  const bool forced = fe && *fe && sscanf(fe, "%d,%d", &f_c, &f_np) == 2;
   const int token_tiles = (T + 2 * kGemmBM - 1) / (2 * kGemmBM);
-  for (int np = 32; np <= 256; np += 32) {
-    GemmPlan p{};
-    p.BN = np;
-    p.token_tiles = token_tiles;
-    p.n_tiles = 2 * ((N + np - 1) / np);
-    p.num_kb = num_kb;
-    const int stage = kGemmBM * kGemmBK * 2 + (np / 2) * kGemmBK * 2;
-    const int extra = 4 * kGemmBM * 64 + 512;
-    p.stages = std::min(kGemmMaxStages, (kPairSmemBudget - 1024 - extra) / stage);
-    p.smem = 1024 + p.stages * stage + extra;
-    int cols = 32;
-    while (cols < np) cols <<= 1;
-    p.tmem_cols = 2 * cols;
-    // the ring receives the other member's partial of ceil(NP/32 / 2) chunks
-    if ((long long)p.stages * stage < (long long)((np / 32 + 1) / 2) * kChunkFloats * 4) continue;
-    if ((*rc = ensure_smem(ds, 8u, gemm_pair_tcgen05_kernel, p.smem))) return best;
-    const long long tiles = (long long)(p.n_tiles / 2) * token_tiles;
-    p.sched = 0;
-    p.csplit = 2;
-    p.splits = (int)(2 * tiles);
-    best = p;
-    if (tiles * 4 <= pair_resident(2, p.smem)) {  // every cluster resident at once
-      *resident = true;
-      break;
+  for (int c = 2; c <= 4; ++c) {
+    if (num_kb < c || (forced && c != f_c)) continue;
+    for (int np = 32; np <= 256; np += 32) {
+      if (forced && np != f_np) continue;
+      GemmPlan p{};
+      p.BN = np;
+      p.token_tiles = token_tiles;
+      p.n_tiles = 2 * ((N + np - 1) / np);
+      p.num_kb = num_kb;
+      const int stage = kGemmBM * kGemmBK * 2 + (np / 2) * kGemmBK * 2;
+      const int extra = 4 * kGemmBM * 64 + 512;
+      p.stages = std::min(kGemmMaxStages, (kPairSmemBudget - 1024 - extra) / stage);
+      p.smem = 1024 + p.stages * stage + extra;
+      int cols = 32;
+      while (cols < np) cols <<= 1;
+      p.tmem_cols = 2 * cols;
+      // the ring receives ceil(NP/32 / C) chunks from each of the C - 1 others
+      const int nchunks = np / 32;
+      const long long recv = (long long)((nchunks + c - 1) / c) * (c - 1) * kChunkFloats * 4;
+      if ((long long)p.stages * stage < recv) continue;
+      if ((*rc = ensure_smem(ds, 8u, gemm_pair_tcgen05_kernel, p.smem))) return GemmPlan{};
+      const long long tiles = (long long)(p.n_tiles / 2) * token_tiles;
+      const bool all_resident = tiles * 2 * c <= pair_resident(c, p.smem);
+      if (!all_resident && !forced) continue;
+      p.sched = 0;
+      p.csplit = c;
+      p.splits = (int)(c * tiles);
+      const double kb_share = (double)((num_kb + c - 1) / c);
+      const double cost = kb_share * (double)stage / 74e3 + (double)recv / 150e3 + 1.0;  // us
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = p;
+        *resident = all_resident;
+      }
     }
   }
   if (gemm_debug() && best.splits)
-    fprintf(stderr, "[b200 gemm pair] T=%d N=%d K=%d NP=%d tiles=%d kb=%d cluster split-K pairs=%d smem=%d\n", T,
-            N, K, best.BN, best.n_tiles / 2 * best.token_tiles, best.num_kb, best.splits, best.smem);
+    fprintf(stderr, "[b200 gemm pair] T=%d N=%d K=%d NP=%d tiles=%d kb=%d cluster split-K C=%d pairs=%d smem=%d cost=%.1f\n",
+            T, N, K, best.BN, best.n_tiles / 2 * best.token_tiles, best.num_kb, best.csplit, best.splits,
+            best.smem, best_cost);
   return best;
 }
 
@@ -512,7 +524,7 @@ int launch_pair(const GemmPlan& p, const CUtensorMap& tmW, const CUtensorMap& tm
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.csplit == 2 ? 4 : 2;
+  attr[0].val.clusterDim.x = p.csplit >= 2 ? 2 * p.csplit : 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1012,6 +1024,94 @@ int b200_argmax(const void* logits, long long stride, int rows, int V, long long
   return check_launch("argmax_kernel");
 }
 
+int b200_select_tokens_partial(const void* logits, long long stride, int rows, int V,
+                               long long vocab_start, const float* temperatures, const float* noise,
+                               long long noise_stride, unsigned long long seed,
+                               unsigned long long offset, long long* keys, b200_stream_t stream) {
+  if (rows <= 0) return B200_OK;
+  if (V <= 0 || !logits || !keys || vocab_start < 0 || vocab_start + V > 0xFFFFFFFFll || stride < V ||
+      (noise && noise_stride < V))
+    return fail(B200_ERR_INVALID, "select_tokens_partial: rows=%d V=%d vocab_start=%lld", rows, V, vocab_start);
+  SelectArgs a{};
+  a.logits = static_cast<const __nv_bfloat16*>(logits);
+  a.stride = stride;
+  a.rows = rows;
+  a.V = V;
+  a.vocab_start = vocab_start;
+  a.temperatures = temperatures;
+  a.noise = noise;
+  a.noise_stride = noise_stride;
+  a.seed = seed;
+  a.offset = offset;
+  a.keys = keys;
+  launch_ex(token_select_kernel, dim3(rows), dim3(1024), 0, reinterpret_cast<cudaStream_t>(stream), nullptr, 0,
+            a);
+  return check_launch("token_select_kernel");
+}
+
+namespace {
+int exchange_args(int rank, int world, void* const* key_slots, void* const* flags, void* state,
+                  long long max_rows, ExchangeArgs* x) {
+  if (world < 1 || world > kXchgMaxRanks || rank < 0 || rank >= world || (world > 1 && (!flags || !state)))
+    return fail(B200_ERR_INVALID, "exchange: rank %d / world %d / buffers", rank, world);
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  *x = ExchangeArgs{};
+  x->rank = rank;
+  x->world = world;
+  x->max_rows = max_rows;
+  x->state = static_cast<unsigned*>(state);
+  x->err = ds->err;
+  for (int r = 0; r < world && world > 1; ++r) {
+    if (!flags[r]) return fail(B200_ERR_PEER, "exchange: flags of rank %d missing", r);
+    x->flags[r] = static_cast<unsigned*>(flags[r]);
+    if (key_slots) {
+      if (!key_slots[r]) return fail(B200_ERR_PEER, "exchange: key slots of rank %d missing", r);
+      x->key_slots[r] = static_cast<long long*>(key_slots[r]);
+    }
+  }
+  return B200_OK;
+}
+}  // namespace
+
+int b200_select_tokens_exchange(const long long* keys, int rows, int rank, int world,
+                                void* const* key_slots, void* const* flags, void* state,
+                                long long max_rows, long long* tokens, b200_stream_t stream) {
+  if (rows <= 0) return B200_OK;
+  if (!keys || !tokens || rows > 1024 || (world > 1 && (!key_slots || rows > max_rows)))
+    return fail(B200_ERR_INVALID, "select_tokens_exchange: %d rows (at most 1024 and max_rows %lld)", rows,
+                max_rows);
+  ExchangeArgs x;
+  if (int r = exchange_args(rank, world, key_slots, flags, state, max_rows, &x)) return r;
+  launch_ex(keys_exchange_kernel, dim3(1), dim3(1024), 0, reinterpret_cast<cudaStream_t>(stream), nullptr, 0,
+            keys, rows, tokens, x);
+  return check_launch("keys_exchange_kernel");
+}
+
+int b200_embedding_exchange(const long long* ids, const void* weight, int T, int H, long long vocab_start,
+                            long long vocab_end, long long vocab_size, int rank, int world,
+                            void* const* out, long long ld_out, void* const* flags, void* state,
+                            b200_stream_t stream) {
+  if (T <= 0) return B200_OK;
+  if (!ids || !weight || !out || H <= 0 || H % 8 || ld_out % 8 || ld_out < H || !aligned16(weight))
+    return fail(B200_ERR_INVALID, "embedding_exchange: H=%d ld_out=%lld", H, ld_out);
+  ExchangeArgs x;
+  if (int r = exchange_args(rank, world, nullptr, flags, state, 0, &x)) return r;
+  __nv_bfloat16* const* outs = reinterpret_cast<__nv_bfloat16* const*>(out);
+  for (int r = 0; r < world; ++r)
+    if (!outs[r] || !aligned16(outs[r])) return fail(B200_ERR_PEER, "embedding_exchange: output of rank %d", r);
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  const long long vecs = (long long)T * (H / 8);
+  const int blocks = (int)std::min<long long>((vecs + 255) / 256, (long long)ds->num_sms * 4);
+  EmbeddingOuts o{};
+  for (int r = 0; r < world; ++r) o.p[r] = outs[r];
+  launch_ex(embedding_exchange_kernel, dim3(blocks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), nullptr,
+            0, ids, static_cast<const __nv_bfloat16*>(weight), T, H, vocab_start, vocab_end, vocab_size, o, ld_out,
+            x);
+  return check_launch("embedding_exchange_kernel");
+}
+
 int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_t* bytes) {
   if (!bytes || max_seqs < 0 || max_seqlen_k < 0 || Hq <= 0)
     return fail(B200_ERR_INVALID, "bad arguments");
@@ -1070,7 +1170,6 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
     a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
     a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
     a.err = ds->err;
-    a.p_lo = decode_p_lo();
     const int smem = dec_smem_bytes();
     if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
     if (int r = launch_decode(ds, tmK, tmV, tmQ, a, smem, st)) return r;
@@ -1271,7 +1370,6 @@ extern "C" int b200_paged_decode_attention_static(
   a.part_o = a.part_ml + (size_t)a.cap_items * Hq * 2;
   a.out = static_cast<__nv_bfloat16*>(out); a.out_stride = out_stride;
   a.err = ds->err;
-  a.p_lo = decode_p_lo();
   const int smem = dec_smem_bytes();
   if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
   if (int r = launch_decode(ds, tmK, tmV, tmQ, a, smem, st)) return r;

@@ -69,7 +69,6 @@ struct DecodeArgs {
   __nv_bfloat16* out;
   long long out_stride;
   unsigned* err;
-  int p_lo;              // 1: P enters the PV MMAs as bf16 hi + lo parts (fp32-exact P)
 };
 
 struct DecTile {
@@ -368,12 +367,10 @@ __global__ void __launch_bounds__(128, 1)
       alpha[e] = m_run[e] == -INFINITY ? 0.f : fast_exp2(m_run[e] - m_new[e]);
       m_run[e] = m_new[e];
     }
-    // P -> B fragments of P^T through 8x8 transposes.  P enters the PV MMA
-    // as bf16 hi + lo parts (p_lo), which keeps it exact to ~2^-17 as in an
-    // fp32 softmax; with p_lo == 0 only the bf16 hi part is used, the operand
-    // rounding of flash attention's PV product.
+    // P (bf16, as the PV operand of the reference's flash attention) ->
+    // B fragments of P^T through 8x8 transposes
     float ls[2] = {0.f, 0.f};
-    uint32_t pb[2][2], pl[2][2];
+    uint32_t pb[2][2];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
       float pv[4];
@@ -382,15 +379,8 @@ __global__ void __launch_bounds__(128, 1)
         pv[i] = m_new[i & 1] == -INFINITY ? 0.f : fast_exp2(sc[mt][i] - m_new[i & 1]);
         ls[i & 1] += pv[i];
       }
-      const uint32_t h01 = pack_bf16x2(pv[0], pv[1]);  // tokens 16mt + 2tq, +1
-      const uint32_t h23 = pack_bf16x2(pv[2], pv[3]);  // tokens 16mt + 8 + 2tq, +1
-      pb[mt][0] = movmatrix_trans(h01);
-      pb[mt][1] = movmatrix_trans(h23);
-      if (a.p_lo) {
-        const float2 f01 = unpack_bf16x2(h01), f23 = unpack_bf16x2(h23);
-        pl[mt][0] = movmatrix_trans(pack_bf16x2(pv[0] - f01.x, pv[1] - f01.y));
-        pl[mt][1] = movmatrix_trans(pack_bf16x2(pv[2] - f23.x, pv[3] - f23.y));
-      }
+      pb[mt][0] = movmatrix_trans(pack_bf16x2(pv[0], pv[1]));  // tokens 16mt + 2tq, +1
+      pb[mt][1] = movmatrix_trans(pack_bf16x2(pv[2], pv[3]));  // tokens 16mt + 8 + 2tq, +1
     }
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
@@ -413,7 +403,6 @@ __global__ void __launch_bounds__(128, 1)
         ldmatrix_x4_trans(sV + tswz(4096, 16 * ks + (lane & 7) + 8 * (lane >> 4), 2 * md + ((lane >> 3) & 1)),
                           va[0], va[1], va[2], va[3]);
         mma_bf16_16816(ot[md], va, pb[ks][0], pb[ks][1]);
-        if (a.p_lo) mma_bf16_16816(ot[md], va, pl[ks][0], pl[ks][1]);
       }
     }
 

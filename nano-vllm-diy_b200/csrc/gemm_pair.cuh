@@ -180,14 +180,15 @@ __device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs
 // members, and for w >= 1 it overlaps the MMAs of the next whole tile.  The
 // last member to finish resets the group's flags for the next launch.
 //
-// Cluster split-K (p.csplit = 2; plain epilogue only): clusters of 4 CTAs =
-// 2 pairs and one tile per cluster; member m = cluster rank / 2 computes K
-// blocks [m nkb / 2, (m + 1) nkb / 2).  Member m owns the 32-wide output
-// chunks c with c % 2 == m.  After a cluster barrier (every ring of the
-// cluster is idle) each CTA pushes the chunks the other member owns from
-// TMEM straight into that member's stage ring (st.async, counted on its
-// mbarrier), then sums its own chunks from TMEM and the pushed partials and
-// writes them: no L2 round trip and no flags.
+// Cluster split-K (p.csplit = C in 2..4; plain epilogue only): clusters of
+// 2C CTAs = C pairs and one tile per cluster; member m = cluster rank / 2
+// computes K blocks [m nkb / C, (m + 1) nkb / C).  Member m owns the 32-wide
+// output chunks c with c % C == m.  After a cluster barrier (every ring of the
+// cluster is idle) each CTA pushes the chunks other members own from TMEM
+// straight into the owner's stage ring (st.async, counted on the owner's
+// mbarrier; slot (c / C) (C - 1) + the sender's index among the owner's
+// peers), then sums its own chunks from TMEM and the pushed partials (members
+// in rank order) and writes them: no L2 round trip and no flags.
 // ---------------------------------------------------------------------------
 
 // One segment of a pair's work: K blocks [kbb, kbe) of `tile`; `member` is
@@ -283,15 +284,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int pairs = gridDim.x >> 1;
   const long long tiles = (long long)p.tiles_m * p.tiles_t;
   const long long total = tiles * p.num_kb;
-  const bool csk = p.csplit == 2;     // cluster split-K
-  const int cmem = (int)(crank >> 1);  // cluster split-K: member index (0, 1)
+  const int C = p.csplit;              // cluster split-K: pairs per tile (0: off)
+  const bool csk = C >= 2;
+  const int cmem = (int)(crank >> 1);  // cluster split-K: member index (0 .. C - 1)
   // stream-K: this pair's units (unused by the grouped schedule); cluster
-  // split-K: this member's half of the cluster's tile (one segment)
+  // split-K: this member's share of the cluster's tile (one segment)
   long long u_begin, u_end;
   if (csk) {
-    const long long t0 = (long long)(blockIdx.x >> 2) * p.num_kb;
-    u_begin = t0 + (long long)cmem * p.num_kb / 2;
-    u_end = t0 + (long long)(cmem + 1) * p.num_kb / 2;
+    const long long t0 = (long long)(blockIdx.x / (2 * C)) * p.num_kb;
+    u_begin = t0 + (long long)cmem * p.num_kb / C;
+    u_end = t0 + (long long)(cmem + 1) * p.num_kb / C;
   } else {
     u_begin = sk_begin(total, pr, pairs);
     u_end = sk_begin(total, pr + 1, pairs);
@@ -506,36 +508,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     };
     if (csk) {
       // ---- cluster split-K (see the schedule notes above).  The other
-      // member pushes its partial of this CTA's output chunks (c % 2 == cmem)
-      // into ring slots c / 2: arm the byte count before the barrier.
-      const int n_own = (nchunks - cmem + 1) / 2;
-      if (lead_thread) mbar_arrive_expect_tx(&fix_bar[0], (uint32_t)n_own * kChunkFloats * 4);
+      // members push their partials of this CTA's output chunks (c % C ==
+      // cmem) into its ring: arm the byte count before the barrier.
+      const int n_own = cmem < nchunks ? (nchunks - cmem + C - 1) / C : 0;
+      if (lead_thread) mbar_arrive_expect_tx(&fix_bar[0], (uint32_t)(n_own * (C - 1)) * kChunkFloats * 4);
       const bool have = mbar_wait(&acc_full[0], 0u, p.err);
       tc_fence_before();
       cluster_arrive();
       cluster_wait();  // every pair of the cluster has finished its MMAs: every ring is idle
       tc_fence_after();
       const uint32_t d = tmem_base + ((uint32_t)(q * 32) << 16);
-      const uint32_t peer = (uint32_t)((1 - cmem) * 2) + v;  // the other member, same token half
-      const uint32_t peer_ring = map_to_rank(smem_u32(smem), peer) + (uint32_t)row * 16u;
-      const uint32_t peer_bar = map_to_rank(smem_u32(&fix_bar[0]), peer);
-      for (int c = 1 - cmem; c < nchunks; c += 2) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(d + (uint32_t)(c * 32), r);
-        tmem_ld_wait_regs(r);
-        const uint32_t dst = peer_ring + (uint32_t)(c / 2) * (uint32_t)(kChunkFloats * 4);
+      const uint32_t my_ring = smem_u32(smem) + (uint32_t)row * 16u;
+      const uint32_t my_bar = smem_u32(&fix_bar[0]);
+      // push the chunks owned by the other members, the next TMEM load
+      // overlapping this chunk's remote stores
+      auto next_push = [&](int c) {
+        do {
+          ++c;
+        } while (c < nchunks && c % C == cmem);
+        return c;
+      };
+      {
+        uint32_t rc[32], rn[32];
+        int c = next_push(-1);
+        if (c < nchunks) {
+          tmem_ld_32x32b_x32(d + (uint32_t)(c * 32), rc);
+          tmem_ld_wait_regs(rc);
+        }
+        while (c < nchunks) {
+          const int nx = next_push(c);
+          if (nx < nchunks) tmem_ld_32x32b_x32(d + (uint32_t)(nx * 32), rn);
+          const int owner = c % C;
+          const uint32_t peer = (uint32_t)(owner * 2) + v;  // the owner, same token half
+          const int slot = (c / C) * (C - 1) + (cmem < owner ? cmem : cmem - 1);
+          const uint32_t dst = map_to_rank(my_ring, peer) + (uint32_t)slot * (uint32_t)(kChunkFloats * 4);
+          const uint32_t bar = map_to_rank(my_bar, peer);
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          st_async_v4(dst + (uint32_t)(j * kGemmBM * 16), r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3],
-                      peer_bar);
+          for (int j = 0; j < 8; ++j)
+            st_async_v4(dst + (uint32_t)(j * kGemmBM * 16), rc[4 * j], rc[4 * j + 1], rc[4 * j + 2],
+                        rc[4 * j + 3], bar);
+          if (nx < nchunks) tmem_ld_wait_regs(rn);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) rc[j] = rn[j];
+          c = nx;
+        }
       }
       const bool got = mbar_wait_cluster(&fix_bar[0], 0u, p.err);
-      const long long tile = blockIdx.x >> 2;
+      const long long tile = blockIdx.x / (2 * C);
       const int mt = (int)(tile / p.tiles_t);
       const int tt = (int)(tile - (long long)mt * p.tiles_t);
       const int row0 = tt * 2 * kGemmBM + (int)v * kGemmBM;
       const int tok = row0 + row;
-      for (int c = cmem; c < nchunks; c += 2) {
+      for (int c = cmem; c < nchunks; c += C) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(d + (uint32_t)(c * 32), r);
         tmem_ld_wait_regs(r);
@@ -543,12 +567,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = have ? __uint_as_float(r[j]) : 0.f;
         if (got) {
-          // own + other member (fp32 addition commutes: the same sum on both owners)
-          const float4* src = reinterpret_cast<const float4*>(smem + (size_t)(c / 2) * kChunkFloats * 4) + row;
+          // own partial, then the other members' in rank order (one owner
+          // per chunk: a fixed summation order)
+          for (int si = 0; si < C - 1; ++si) {
+            const float4* src =
+                reinterpret_cast<const float4*>(smem + (size_t)((c / C) * (C - 1) + si) * kChunkFloats * 4) + row;
+            float4 f[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 f = src[j * kGemmBM];
-            acc[4 * j] += f.x; acc[4 * j + 1] += f.y; acc[4 * j + 2] += f.z; acc[4 * j + 3] += f.w;
+            for (int j = 0; j < 8; ++j) f[j] = src[j * kGemmBM];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              acc[4 * j] += f[j].x; acc[4 * j + 1] += f[j].y; acc[4 * j + 2] += f[j].z; acc[4 * j + 3] += f[j].w;
+            }
           }
         }
         const int f0 = mt * NP + c * 32;

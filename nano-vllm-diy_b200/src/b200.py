@@ -60,6 +60,12 @@ _SIGNATURES = {
     "b200_silu_and_mul": ([_c_void_p, _ll, _c_void_p, _ll, _i, _i, _c_void_p], _i),
     "b200_embedding": ([_c_void_p, _c_void_p, _c_void_p, _i, _i, _ll, _ll, _c_void_p], _i),
     "b200_argmax": ([_c_void_p, _ll, _i, _i, _c_void_p, _c_void_p], _i),
+    "b200_embedding_exchange": ([_c_void_p, _c_void_p, _i, _i, _ll, _ll, _ll, _i, _i, _c_void_p, _ll,
+                                 _c_void_p, _c_void_p, _c_void_p], _i),
+    "b200_select_tokens_partial": ([_c_void_p, _ll, _i, _i, _ll, _c_void_p, _c_void_p, _ll,
+                                    ctypes.c_ulonglong, ctypes.c_ulonglong, _c_void_p, _c_void_p], _i),
+    "b200_select_tokens_exchange": ([_c_void_p, _i, _i, _i, _c_void_p, _c_void_p, _c_void_p, _ll,
+                                     _c_void_p, _c_void_p], _i),
     "b200_attention_workspace_bytes": ([_i, _i, _i, ctypes.POINTER(_sz)], _i),
     "b200_paged_decode_attention_static": ([_c_void_p, _ll, _i, _c_void_p, _c_void_p, _ll,
                                             _c_void_p, _i, _i, _c_void_p, _c_void_p, _i, _i,
@@ -524,3 +530,74 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     out = torch.empty(rows, dtype=torch.int64, device=logits.device)
     _check(lib.b200_argmax(_p(logits), logits.stride(0), rows, V, _p(out), _stream()), "b200_argmax")
     return out
+
+
+# ---------------------------------------------------------------------------
+# vocabulary-parallel token selection and embedding exchange
+# ---------------------------------------------------------------------------
+def select_tokens(logits: torch.Tensor, vocab_start: int = 0,
+                  temperatures: torch.Tensor | None = None, noise: torch.Tensor | None = None,
+                  seed: int = 0, offset: int = 0) -> torch.Tensor:
+    """Packed (score, global index) key of each row's best column of this
+    vocabulary shard: greedy without `temperatures`, else the Gumbel-max form
+    of src/layers/sampler.py:4-17 (Exp(1) draws from `noise`, or Philox keyed
+    by seed / offset).  int64 [rows]."""
+    lib = load_library()
+    _cuda(logits, temperatures, noise)
+    _bf16(logits)
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    rows, V = logits.shape
+    if temperatures is not None:
+        if temperatures.dtype != torch.float32 or temperatures.shape != (rows,):
+            raise TypeError("temperatures must be float32 [rows]")
+        temperatures = temperatures.contiguous()
+    if noise is not None:
+        if noise.dtype != torch.float32 or noise.shape != (rows, V) or noise.stride(-1) != 1:
+            raise TypeError("noise must be float32 [rows, V] with contiguous rows")
+    keys = torch.empty(rows, dtype=torch.int64, device=logits.device)
+    _check(lib.b200_select_tokens_partial(_p(logits), logits.stride(0), rows, V, int(vocab_start),
+                                          _p(temperatures), _p(noise),
+                                          noise.stride(0) if noise is not None else 0,
+                                          int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1),
+                                          _p(keys), _stream()), "b200_select_tokens_partial")
+    return keys
+
+
+def tokens_from_keys(keys: torch.Tensor, rank: int = 0, world: int = 1,
+                     key_slots: list[int] | None = None, flags: list[int] | None = None,
+                     state: int | None = None, max_rows: int = 0,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tokens int64 [rows]: the maximum key of each row over the ranks (the
+    exchange needs the symmetric buffers at world > 1)."""
+    lib = load_library()
+    _cuda(keys)
+    rows = keys.numel()
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=keys.device)
+    arr = ctypes.c_void_p * max(world, 1)
+    ks = arr(*key_slots) if key_slots else None
+    fl = arr(*flags) if flags else None
+    _check(lib.b200_select_tokens_exchange(_p(keys), rows, rank, world, ks, fl,
+                                           ctypes.c_void_p(state) if state else None, max_rows,
+                                           _p(out), _stream()), "b200_select_tokens_exchange")
+    return out
+
+
+def embedding_exchange(ids: torch.Tensor, weight: torch.Tensor, vocab_start: int, vocab_end: int,
+                       vocab_size: int, rank: int, world: int, outs: list[int], ld_out: int,
+                       flags: list[int] | None, state: int | None) -> None:
+    """Rows of `ids` from every rank's vocabulary shard into outs[rank] of
+    every rank (src/layers/llm_head.py:38-49 with its all-reduce)."""
+    lib = load_library()
+    _cuda(ids, weight)
+    _bf16(weight)
+    if ids.dtype != torch.int64:
+        ids = ids.to(torch.int64)
+    ids = ids.contiguous()
+    arr = ctypes.c_void_p * world
+    _check(lib.b200_embedding_exchange(_p(ids), _p(weight), ids.numel(), weight.shape[1],
+                                       int(vocab_start), int(vocab_end), int(vocab_size), rank, world,
+                                       arr(*outs), ld_out, arr(*flags) if flags else None,
+                                       ctypes.c_void_p(state) if state else None, _stream()),
+           "b200_embedding_exchange")

@@ -21,7 +21,6 @@ import torch
 
 from src import b200
 from src.engine import metadata as M
-from src.layers.sampler import greedy
 from src.models.qwen3 import Qwen3ForCausalLM
 from src.utils.context import Context
 from src.utils.loader import load_weights
@@ -98,11 +97,13 @@ class ModelRunner:
         return M.to_device(M.build(seqs, self.block_size), self.device)
 
     @torch.inference_mode()
-    def run_model(self, input_ids: torch.Tensor, positions: torch.Tensor, ctx: Context) -> torch.Tensor:
-        """Logits [B, V] (rank 0; None on other ranks at tp > 1)."""
+    def run_hidden(self, input_ids: torch.Tensor, positions: torch.Tensor,
+                   ctx: Context) -> tuple[torch.Tensor, Context]:
+        """Final hidden states and the context the LM head takes: eager for
+        prefill / mixed batches, the captured graph for pure decode."""
         bs = input_ids.size(0)
         if ctx.max_seqlen_q != 1 or self.enforce_eager or not self.graphs or bs > max(self.graphs):
-            return self.model.compute_logits(self.model(input_ids, positions, ctx), ctx)
+            return self.model(input_ids, positions, ctx), ctx
         gbs = next(x for x in sorted(self.graphs) if x >= bs)
         v = self.graph_vars
         v["input_ids"][:bs] = input_ids
@@ -116,23 +117,38 @@ class ModelRunner:
         v["block_tables"].fill_(-1)
         v["block_tables"][:bs, :ctx.block_tables.size(1)] = ctx.block_tables
         self.graphs[gbs].replay()
-        dctx = Context(is_prefill=False)
-        return self.model.compute_logits(v["outputs"][:bs], dctx)
+        return v["outputs"][:bs], Context(is_prefill=False)
+
+    @torch.inference_mode()
+    def run_model(self, input_ids: torch.Tensor, positions: torch.Tensor, ctx: Context) -> torch.Tensor:
+        """Logits [B, V] (rank 0; None on other ranks at tp > 1)."""
+        hidden, hctx = self.run_hidden(input_ids, positions, ctx)
+        return self.model.compute_logits(hidden, hctx)
+
+    @torch.inference_mode()
+    def step_tokens(self, seqs, temperatures: torch.Tensor | None = None, seed: int = 0,
+                    offset: int = 0) -> list[int]:
+        """prepare -> forward -> one token per sequence on every rank, selected
+        from the ranks' vocabulary shards (greedy without temperatures)."""
+        ids, pos, ctx = self.prepare(seqs)
+        hidden, hctx = self.run_hidden(ids, pos, ctx)
+        if temperatures is not None:
+            temperatures = temperatures.to(device=self.device, dtype=torch.float32)
+        return self.model.lm_head.select_tokens(hidden, hctx, temperatures, seed=seed,
+                                                offset=offset).tolist()
 
     @torch.inference_mode()
     def step_greedy(self, seqs) -> list[int]:
-        """prepare -> forward -> greedy token per sequence (rank 0)."""
-        ids, pos, ctx = self.prepare(seqs)
-        logits = self.run_model(ids, pos, ctx)
-        return greedy(logits).tolist() if logits is not None else None
+        """prepare -> forward -> greedy token per sequence."""
+        return self.step_tokens(seqs)
 
     # ------------------------------------------------------------------ graphs
     @torch.inference_mode()
     def capture_cudagraph(self, batch_sizes: list[int] | None = None,
                           with_sampling: bool = False) -> None:
         """Capture the decode forward for each batch size.  With
-        `with_sampling` the graph also runs the LM head and greedy argmax,
-        leaving the tokens in graph_vars["tokens"] (rank 0)."""
+        `with_sampling` the graph also runs the LM head and the greedy token
+        selection, leaving the tokens in graph_vars["tokens"] (every rank)."""
         max_bs = min(self.max_num_seqs, 512)
         if batch_sizes is None:
             batch_sizes = [b for b in [1, 2, 4, 8] + list(range(16, max_bs + 1, 16)) if b <= max_bs]
@@ -159,9 +175,8 @@ class ModelRunner:
             def step():
                 v["outputs"][:bs] = self.model(v["input_ids"][:bs], v["positions"][:bs], ctx)
                 if with_sampling:
-                    logits = self.model.compute_logits(v["outputs"][:bs], Context(is_prefill=False))
-                    if logits is not None:
-                        v["tokens"][:bs] = greedy(logits)
+                    v["tokens"][:bs] = self.model.lm_head.select_tokens(v["outputs"][:bs],
+                                                                        Context(is_prefill=False))
 
             step()  # warm-up outside the graph
             graph = torch.cuda.CUDAGraph()

@@ -18,10 +18,22 @@ Symmetric memory: every rank allocates one device buffer holding
   stage  bf16 [halves][world][max_tokens][ldo]  partials received
   out    bf16 [2][max_tokens][ldo]              reduced outputs (ping-pong)
   flags  uint32 [halves][MAX_POSITIONS], done uint32 [MAX_POSITIONS]
+  keys   int64 [2][world][max_tokens]           token-selection keys received
+  emb    bf16 [2][max_tokens][ldo]              embedding rows (ping-pong)
+  xflags uint32 [2][8], xstate uint32 [4]       exchange epochs and counter
 with halves = 2 for one-shot (alternating by call parity), 1 for two-shot,
 and exchanges its CUDA IPC handle through the default process group (after
 init_process_group, outside graph capture), so every rank knows every
 rank's address of each part.
+
+The same buffers carry the decode step's two other exchanges:
+  * the vocabulary-parallel embedding (src/layers/llm_head.py:38-49): the
+    rank owning a token's row writes it into every rank's `emb` rows, one
+    signal round, instead of a masked lookup + NCCL all_reduce;
+  * token selection (src/layers/llm_head.py:60-69 + sampler.py:4-17): every
+    rank selects over its own vocabulary shard and only a packed (score,
+    index) key per sequence crosses NVLink, instead of gathering the
+    [B, V/tp] logits to rank 0.
 
 The returned tensor is a view of an output buffer that the call after the
 next one overwrites (two buffers alternate), which is how the decoder
@@ -71,7 +83,15 @@ class FusedRowParallel:
         self.off_out = [self.stage_bytes, self.stage_bytes + self.out_bytes]
         self.off_flags = self.stage_bytes + 2 * self.out_bytes
         self.off_done = self.off_flags + flag_bytes
-        total = self.off_done + flag_bytes
+
+        def up(n):
+            return (n + 255) // 256 * 256
+        self.off_keys = up(self.off_done + flag_bytes)
+        self.off_emb = [up(self.off_keys + 2 * self.world * max_tokens * 8)]
+        self.off_emb.append(self.off_emb[0] + self.out_bytes)
+        self.off_xflags = up(self.off_emb[1] + self.out_bytes)
+        self.off_xstate = self.off_xflags + 256
+        total = self.off_xstate + 256
         self.buf = torch.zeros(total, dtype=torch.uint8, device=device)
         handle, offset = b200.ipc_export(self.buf)
         gathered = [None] * self.world
@@ -87,6 +107,9 @@ class FusedRowParallel:
                 self.bases.append(ptr)
         self.outs = [self.buf[o:o + self.out_bytes].view(torch.bfloat16).view(max_tokens, self.ldo)
                      for o in self.off_out]
+        self.embs = [self.buf[o:o + self.out_bytes].view(torch.bfloat16).view(max_tokens, self.ldo)
+                     for o in self.off_emb]
+        self._eflip = 0
         self._flip = 0
         self.fused_calls = 0
         self.fallback_calls = 0
@@ -142,6 +165,35 @@ class FusedRowParallel:
         y = b200.linear(x, w, bias)
         dist.all_reduce(y, group=self.group)
         return y
+
+    # ------------------------------------------------------------ exchanges
+    def can_exchange(self, rows: int, width: int = 0) -> bool:
+        """Whether `rows` tokens of `width` features fit the exchange buffers
+        (a shape condition: the same answer on every rank)."""
+        return 0 < rows <= self.max_tokens and width <= self.ldo
+
+    def embedding(self, ids: torch.Tensor, weight: torch.Tensor, vocab_start: int, vocab_end: int,
+                  vocab_size: int) -> torch.Tensor:
+        """VocabParallelEmbedding.forward with its all_reduce (llm_head.py:38-49):
+        [T, H], a view of this rank's embedding rows (two buffers alternate;
+        a call overwrites the buffer of the call before last)."""
+        T, H = ids.numel(), weight.shape[1]
+        idx = self._eflip
+        b200.embedding_exchange(ids, weight, vocab_start, vocab_end, vocab_size, self.rank, self.world,
+                                self._addrs(self.off_emb[idx]), self.ldo, self._addrs(self.off_xflags),
+                                self.bases[self.rank] + self.off_xstate)
+        self._eflip ^= 1
+        return self.embs[idx][:T, :H]
+
+    def select_tokens(self, logits: torch.Tensor, vocab_start: int,
+                      temperatures: torch.Tensor | None = None, noise: torch.Tensor | None = None,
+                      seed: int = 0, offset: int = 0) -> torch.Tensor:
+        """Token per row over the whole vocabulary from this rank's logits
+        shard [B, V/tp]: the same int64 [B] on every rank."""
+        keys = b200.select_tokens(logits, vocab_start, temperatures, noise, seed, offset)
+        return b200.tokens_from_keys(keys, self.rank, self.world, self._addrs(self.off_keys),
+                                     self._addrs(self.off_xflags),
+                                     self.bases[self.rank] + self.off_xstate, self.max_tokens)
 
     def close(self) -> None:
         if self.buf is None:

@@ -1,8 +1,11 @@
 """CPU restatements of the reference's layer ops (test infrastructure only).
 
-Each function cites the reference code it restates.  All tensors are CPU
-tensors; bf16 in, bf16 out, fp32 inside, with bf16 rounding at the same points
-as the reference modules.
+Each function cites the reference code it restates.  Tensors are CPU tensors
+(the oracle proper); bf16 in, bf16 out, fp32 inside, with bf16 rounding at the
+same points as the reference modules.  The functions are device-agnostic, so
+a test can also run them on CUDA tensors with NATIVE_BF16_LINEAR set: that is
+the reference's own torch path (bf16 F.linear on cuBLAS, the same module
+composition) on the GPU, a second yardstick beside the CPU oracle.
 """
 from __future__ import annotations
 
@@ -95,7 +98,7 @@ def store_kvcache(key, value, k_cache, v_cache, slot_mapping) -> None:
 def gather_paged(cache: torch.Tensor, block_table_row: torch.Tensor, n: int) -> torch.Tensor:
     """Rows 0..n-1 of one sequence from a [num_blocks, page, Hkv, d] cache."""
     page = cache.shape[1]
-    j = torch.arange(n)
+    j = torch.arange(n, device=cache.device)
     blocks = block_table_row[(j // page)].long()
     return cache[blocks, j % page]
 
@@ -108,7 +111,7 @@ def varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, scale, k_cache=None, v
     come from the paged cache when a block table is given.  Rows with no
     visible key are zero; sequences with Lq <= 0 are skipped.  fp32 softmax."""
     T, Hq, d = q.shape
-    out = torch.zeros(T, Hq, d, dtype=q.dtype)
+    out = torch.zeros(T, Hq, d, dtype=q.dtype, device=q.device)
     B = cu_seqlens_q.numel() - 1
     for b in range(B):
         q0, q1 = int(cu_seqlens_q[b]), int(cu_seqlens_q[b + 1])
@@ -128,8 +131,8 @@ def varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, scale, k_cache=None, v
         kf = kb.float().transpose(0, 1).repeat_interleave(G, 0)      # [Hq, Lk, d]
         vf = vb.float().transpose(0, 1).repeat_interleave(G, 0)
         s = (qf @ kf.transpose(1, 2)) * scale
-        i = torch.arange(Lq)[:, None]
-        j = torch.arange(Lk)[None, :]
+        i = torch.arange(Lq, device=q.device)[:, None]
+        j = torch.arange(Lk, device=q.device)[None, :]
         mask = j <= i + (Lk - Lq)
         s = s.masked_fill(~mask, float("-inf"))
         p = torch.softmax(s, dim=-1)
@@ -137,6 +140,15 @@ def varlen_attention(q, k, v, cu_seqlens_q, cu_seqlens_k, scale, k_cache=None, v
         o = p @ vf
         out[q0:q1] = o.transpose(0, 1).to(q.dtype)
     return out
+
+
+def sample(logits: torch.Tensor, temperatures: torch.Tensor, noise: torch.Tensor) -> torch.Tensor:
+    """src/layers/sampler.py:14-17 with its Exp(1) draws given (`noise`, the
+    tensor `exponential_(1)` fills there): softmax(logits / T) divided by the
+    draws clamped at 1e-10, argmax (first maximum)."""
+    scaled = logits.float() / temperatures.float().unsqueeze(1)
+    probs = torch.softmax(scaled, dim=-1)
+    return (probs / noise.float().clamp_min(1e-10)).argmax(dim=-1)
 
 
 def vocab_embedding(ids: torch.Tensor, w_shard: torch.Tensor, start: int, end: int) -> torch.Tensor:

@@ -78,6 +78,29 @@ def test_linear_kernels_and_splits(T, N, K, kernel, pairs, monkeypatch):
     assert b200.device_error(clear=True) == 0
 
 
+@pytest.mark.parametrize("C,NP", [(2, 192), (2, 256), (3, 256), (3, 128), (4, 256), (4, 96), (3, 64)])
+@pytest.mark.parametrize("T,N,K", [(256, 4096, 4096), (256, 6144, 4096), (200, 1000, 1024),
+                                   (512, 768, 12288), (256, 4096, 12288)])
+def test_linear_cluster_split_k(T, N, K, C, NP, monkeypatch):
+    """The SM-pair kernel's cluster split-K mode with clusters of C pairs (2C
+    CTAs, K split C ways) and NP weight rows per tile, forced: every member
+    pushes the 32-wide chunks the others own into their rings (NP = 96 at
+    C = 4 and NP = 64 at C = 3 leave a member owning nothing)."""
+    from src import b200
+    monkeypatch.setenv("B200_GEMM_PAIR", "3")
+    monkeypatch.setenv("B200_GEMM_CSK", f"{C},{NP}")
+    x = randn(T, K, seed=13)
+    w = randn(N, K, std=0.02, seed=14)
+    ref = x.float() @ w.float().t()
+    y = b200.linear(x.to(DEV), w.to(DEV))
+    torch.cuda.synchronize()
+    assert L.rel_err(y.cpu(), ref) <= 1e-2
+    # the same call again: the rings and barriers start clean every launch
+    y2 = b200.linear(x.to(DEV), w.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+
+
 @pytest.mark.parametrize("kernel,T", [("default", 48), ("grouped", 200), ("streamk", 200), ("cluster", 200)])
 @pytest.mark.parametrize("col0", [0, 1])
 def test_linear_bias_and_strided_out(kernel, T, col0, monkeypatch):

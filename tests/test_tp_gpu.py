@@ -9,6 +9,12 @@ per GPU; each case is skipped when the machine shows fewer GPUs).
 * BASELINE config 1 (x [512, 1536], W [1024, 1536] per rank, world 2, seed
   0) on the fused kernel against the golden rows of the reference's own
   RowParallelLinear under gloo;
+* the vocabulary-parallel embedding as one NVLink exchange, bit-exact
+  against the oracle's lookup of the full table (src/layers/llm_head.py:38-49);
+* token selection over the ranks' vocabulary shards (greedy, and the
+  reference sampler with given Exp(1) draws), the same token on every rank
+  and equal to the oracle's choice over the full logits
+  (src/layers/llm_head.py:60-69, src/layers/sampler.py:4-17);
 * the Qwen3 model at tp = world against the oracle's tp = world forward,
   prefill and CUDA-graph decode steps.
 """
@@ -119,6 +125,46 @@ def _config1_worker(rank, world, port, one_shot):
         dist.destroy_process_group()
 
 
+def _exchange_worker(rank, world, port):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path[:0] = [os.path.dirname(here), os.path.join(os.path.dirname(here), "nano-vllm-diy_b200")]
+    import torch.distributed as dist
+    from oracle import layers as L
+    from src import b200
+    from src.layers.tp_allreduce import FusedRowParallel
+    dev = _init(rank, world, port)
+    comm = FusedRowParallel(dev, max_tokens=512, max_hidden=1024)
+    try:
+        V, H, T, B = 151936, 1024, 300, 256
+        Vs = V // world
+        start = rank * Vs
+        g = torch.Generator().manual_seed(5)
+        table = torch.randn(V, H, generator=g).to(torch.bfloat16)
+        shard = table[start:start + Vs].contiguous().to(dev)
+        for rep in range(3):
+            ids = torch.randint(-2, V + 2, (T,), generator=g)
+            y = comm.embedding(ids.to(dev), shard, start, start + Vs, V)
+            torch.cuda.synchronize()
+            assert torch.equal(y.cpu(), L.vocab_embedding(ids, table, 0, V)), rep
+        logits = (torch.randn(B, V, generator=g) * 2).to(torch.bfloat16)
+        logits[::5, 7] = logits[::5, V - 3] = logits.max() + 1  # ties: the lower index wins
+        local = logits[:, start:start + Vs].contiguous().to(dev)
+        for rep in range(3):
+            tok = comm.select_tokens(local, start)
+            torch.cuda.synchronize()
+            assert torch.equal(tok.cpu(), logits.float().argmax(-1)), rep
+        temps = (torch.rand(B, generator=g) + 0.2).float()
+        noise = torch.empty(B, V).exponential_(1, generator=g)
+        tok = comm.select_tokens(local, start, temps.to(dev), noise[:, start:start + Vs].contiguous().to(dev))
+        torch.cuda.synchronize()
+        assert torch.equal(tok.cpu(), L.sample(logits, temps, noise))
+        assert b200.device_error(clear=True) == 0
+    finally:
+        comm.close()
+        dist.destroy_process_group()
+
+
 def _model_worker(rank, world, port):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -163,6 +209,14 @@ def _model_worker(rank, world, port):
             if rank == 0:
                 err = L.rel_err(logits.cpu(), ref)
                 assert err <= 2e-2, (step, err)
+            # the same step again, tokens selected on the vocabulary shards:
+            # every rank holds rank 0's argmax of the gathered logits
+            toks = runner.step_tokens(seqs)
+            every = [None] * world
+            dist.all_gather_object(every, toks)
+            assert all(t == every[0] for t in every), every
+            if rank == 0:
+                assert toks == logits.float().argmax(-1).tolist()
             for s, t in zip(seqs, ref.float().argmax(-1).tolist()):
                 s.num_cached_tokens = len(s.token_ids)
                 s.token_ids.append(int(t))
@@ -193,6 +247,13 @@ def test_fused_allreduce_config1_matches_reference_golden(one_shot):
     _need(2)
     import torch.multiprocessing as mp
     mp.spawn(_config1_worker, args=(2, _free_port(), one_shot), nprocs=2, join=True)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_embedding_and_token_selection_exchanges(world):
+    _need(world)
+    import torch.multiprocessing as mp
+    mp.spawn(_exchange_worker, args=(world, _free_port()), nprocs=world, join=True)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
