@@ -261,6 +261,21 @@ int b200_paged_decode_attention_static(const void* q, long long q_stride, int nu
                                        int Hkv, int page, float softmax_scale, void* out,
                                        long long out_stride, b200_stream_t stream);
 
+/* Attention metadata of one step from per-sequence values, the expansion of
+ * src/engine/model_runner.py:174-233 (ModelRunner.prepare_seqs) done on the
+ * device.  seq_info = int32 [3][B]: start = min(num_cached_tokens, len - 1),
+ * num_scheduled_tokens, and the length of the sequence's block table (0 for
+ * none, as in warm-up).  block_tables = int32 [B][bt_stride], -1 padded
+ * (bt_stride 0: no sequence has a table).  Writes cu_seqlens_q / _k [B + 1]
+ * (prefix sums of the query lengths and of end = start + length),
+ * context_lens [B] = end, positions int64 [T] = start .. end - 1 per
+ * sequence, and slot_mapping int32 for the tokens of the sequences that have
+ * a table (block_table[p / page] * page + p % page, in token order; a block
+ * missing from the table gives -1 and B200_DEVERR_BAD_INDEX). */
+int b200_step_metadata(const int* seq_info, const int* block_tables, int bt_stride, int B, int page,
+                       long long* positions, int* slot_mapping, int* cu_seqlens_q, int* cu_seqlens_k,
+                       int* context_lens, b200_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Vocabulary
  * ------------------------------------------------------------------------ */
@@ -307,7 +322,7 @@ int b200_select_tokens_partial(const void* logits, long long stride, int rows, i
  * every rank pushes its keys into key_slots[*] (int64 [2][world][max_rows]
  * per rank), one signal round through flags[*] (as for
  * b200_embedding_exchange, the other word), bounded wait, maximum per row.
- * rows <= 1024.  world 1: tokens straight from the keys. */
+ * rows <= max_rows.  world 1: tokens straight from the keys (any rows). */
 int b200_select_tokens_exchange(const long long* keys, int rows, int rank, int world,
                                 void* const* key_slots, void* const* flags, void* state,
                                 long long max_rows, long long* tokens, b200_stream_t stream);

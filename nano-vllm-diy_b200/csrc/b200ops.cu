@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "elementwise.cuh"
 #include "exchange.cuh"
+#include "metadata.cuh"
 #include "gemm.cuh"
 #include "gemm_pair.cuh"
 #include "../../include/b200ops.h"
@@ -1078,8 +1079,8 @@ int b200_select_tokens_exchange(const long long* keys, int rows, int rank, int w
                                 void* const* key_slots, void* const* flags, void* state,
                                 long long max_rows, long long* tokens, b200_stream_t stream) {
   if (rows <= 0) return B200_OK;
-  if (!keys || !tokens || rows > 1024 || (world > 1 && (!key_slots || rows > max_rows)))
-    return fail(B200_ERR_INVALID, "select_tokens_exchange: %d rows (at most 1024 and max_rows %lld)", rows,
+  if (!keys || !tokens || (world > 1 && (!key_slots || rows > max_rows)))
+    return fail(B200_ERR_INVALID, "select_tokens_exchange: %d rows (at most max_rows %lld across ranks)", rows,
                 max_rows);
   ExchangeArgs x;
   if (int r = exchange_args(rank, world, key_slots, flags, state, max_rows, &x)) return r;
@@ -1110,6 +1111,33 @@ int b200_embedding_exchange(const long long* ids, const void* weight, int T, int
             0, ids, static_cast<const __nv_bfloat16*>(weight), T, H, vocab_start, vocab_end, vocab_size, o, ld_out,
             x);
   return check_launch("embedding_exchange_kernel");
+}
+
+int b200_step_metadata(const int* seq_info, const int* block_tables, int bt_stride, int B, int page,
+                       long long* positions, int* slot_mapping, int* cu_seqlens_q, int* cu_seqlens_k,
+                       int* context_lens, b200_stream_t stream) {
+  if (B <= 0) return B200_OK;
+  if (!seq_info || !positions || !cu_seqlens_q || !cu_seqlens_k || !context_lens || page <= 0 ||
+      bt_stride < 0 || (bt_stride > 0 && (!block_tables || !slot_mapping)))
+    return fail(B200_ERR_INVALID, "step_metadata: B=%d page=%d bt_stride=%d", B, page, bt_stride);
+  DeviceState* ds;
+  if (int r = device_state(&ds)) return r;
+  MetaArgs a{};
+  a.start = seq_info;
+  a.lq = seq_info + B;
+  a.nblk = seq_info + 2 * B;
+  a.block_tables = block_tables;
+  a.bt_stride = bt_stride;
+  a.B = B;
+  a.page = page;
+  a.positions = positions;
+  a.slot_mapping = slot_mapping;
+  a.cu_q = cu_seqlens_q;
+  a.cu_k = cu_seqlens_k;
+  a.context_lens = context_lens;
+  a.err = ds->err;
+  launch_ex(step_metadata_kernel, dim3(B), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), nullptr, 0, a);
+  return check_launch("step_metadata_kernel");
 }
 
 int b200_attention_workspace_bytes(int max_seqs, int max_seqlen_k, int Hq, size_t* bytes) {

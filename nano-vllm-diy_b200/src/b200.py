@@ -60,6 +60,8 @@ _SIGNATURES = {
     "b200_silu_and_mul": ([_c_void_p, _ll, _c_void_p, _ll, _i, _i, _c_void_p], _i),
     "b200_embedding": ([_c_void_p, _c_void_p, _c_void_p, _i, _i, _ll, _ll, _c_void_p], _i),
     "b200_argmax": ([_c_void_p, _ll, _i, _i, _c_void_p, _c_void_p], _i),
+    "b200_step_metadata": ([_c_void_p, _c_void_p, _i, _i, _i, _c_void_p, _c_void_p, _c_void_p,
+                            _c_void_p, _c_void_p, _c_void_p], _i),
     "b200_embedding_exchange": ([_c_void_p, _c_void_p, _i, _i, _ll, _ll, _ll, _i, _i, _c_void_p, _ll,
                                  _c_void_p, _c_void_p, _c_void_p], _i),
     "b200_select_tokens_partial": ([_c_void_p, _ll, _i, _i, _ll, _c_void_p, _c_void_p, _ll,
@@ -601,3 +603,34 @@ def embedding_exchange(ids: torch.Tensor, weight: torch.Tensor, vocab_start: int
                                        arr(*outs), ld_out, arr(*flags) if flags else None,
                                        ctypes.c_void_p(state) if state else None, _stream()),
            "b200_embedding_exchange")
+
+
+# ---------------------------------------------------------------------------
+# step metadata
+# ---------------------------------------------------------------------------
+def step_metadata(seq_info: torch.Tensor, block_tables: torch.Tensor | None, page: int,
+                  num_tokens: int, num_slot_tokens: int):
+    """(positions int64 [T], slot_mapping int32 [slot tokens], cu_seqlens_q,
+    cu_seqlens_k int32 [B + 1], context_lens int32 [B]) from the per-sequence
+    int32 [3, B] (start, query length, block-table length) and the -1-padded
+    block tables (src/engine/model_runner.py:174-233 expanded on the device)."""
+    lib = load_library()
+    _cuda(seq_info, block_tables)
+    if seq_info.dtype != torch.int32 or seq_info.dim() != 2 or seq_info.shape[0] != 3:
+        raise TypeError("seq_info must be int32 [3, B]")
+    seq_info = seq_info.contiguous()
+    B = seq_info.shape[1]
+    dev = seq_info.device
+    positions = torch.empty(num_tokens, dtype=torch.int64, device=dev)
+    slots = torch.empty(num_slot_tokens, dtype=torch.int32, device=dev)
+    cu_q = torch.empty(B + 1, dtype=torch.int32, device=dev)
+    cu_k = torch.empty(B + 1, dtype=torch.int32, device=dev)
+    ctx_lens = torch.empty(B, dtype=torch.int32, device=dev)
+    if block_tables is not None:
+        if block_tables.dtype != torch.int32 or block_tables.stride(-1) != 1:
+            raise TypeError("block_tables must be int32 with contiguous rows")
+    _check(lib.b200_step_metadata(_p(seq_info), _p(block_tables),
+                                  block_tables.stride(0) if block_tables is not None else 0, B, page,
+                                  _p(positions), _p(slots), _p(cu_q), _p(cu_k), _p(ctx_lens), _stream()),
+           "b200_step_metadata")
+    return positions, slots, cu_q, cu_k, ctx_lens

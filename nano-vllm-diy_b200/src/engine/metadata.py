@@ -8,8 +8,12 @@ start) / end; slot(p) = block_table[p // block_size] * block_size +
 p % block_size; -1-padded block tables only when some sequence attends to
 cached keys; is_prefill unless every query length is 1.
 
-The arrays are written into pinned host buffers and copied to the device with
-non-blocking copies on the current stream.
+Two builders with the same result:
+  * build + to_device: every array on the host (numpy), six pinned copies;
+  * build_on_device: the host prepares only per-sequence values (start,
+    query length, block-table length: O(B)), the block tables and the token
+    ids; one kernel (b200_step_metadata) expands positions, slot mapping and
+    the prefix sums on the GPU.
 """
 from __future__ import annotations
 
@@ -91,3 +95,52 @@ def to_device(meta: StepMeta, device) -> tuple[torch.Tensor, torch.Tensor, Conte
         block_tables=dev(meta.block_tables) if meta.block_tables is not None else None,
     )
     return dev(meta.input_ids), dev(meta.positions), ctx
+
+
+def build_on_device(seqs, block_size: int, device) -> tuple[torch.Tensor, torch.Tensor, Context]:
+    """The step's (input_ids, positions, Context) with the per-token expansion
+    done by the b200_step_metadata kernel."""
+    from src import b200
+    B = len(seqs)
+    lens = np.fromiter((len(s) for s in seqs), dtype=np.int64, count=B)
+    cached = np.fromiter((s.num_cached_tokens for s in seqs), dtype=np.int64, count=B)
+    lq = np.fromiter((s.num_scheduled_tokens for s in seqs), dtype=np.int64, count=B)
+    nblk = np.fromiter((len(s.block_table) for s in seqs), dtype=np.int64, count=B)
+    start = np.minimum(cached, lens - 1)
+    end = start + lq
+    T = int(lq.sum())
+    ids = np.empty(T, dtype=np.int64)
+    o = 0
+    for i, s in enumerate(seqs):
+        n = int(lq[i])
+        toks = s.token_ids if hasattr(s, "token_ids") else [s[j] for j in range(len(s))]
+        ids[o:o + n] = toks[int(start[i]):int(end[i])]
+        o += n
+    width = int(nblk.max(initial=0))
+    attends_cache = int(end.sum()) > T  # prefix hits / decode (model_runner.py:211-212)
+    info = np.stack([start, lq, nblk]).astype(np.int32)
+    pinned = torch.from_numpy(info).pin_memory()
+    seq_info = pinned.to(device, non_blocking=True)
+    bt_dev = None
+    if width > 0:
+        bt = np.full((B, width), -1, dtype=np.int32)
+        for i, s in enumerate(seqs):
+            if s.block_table:
+                bt[i, :len(s.block_table)] = s.block_table
+        bt_dev = torch.from_numpy(bt).pin_memory().to(device, non_blocking=True)
+    ids_dev = torch.from_numpy(ids).pin_memory().to(device, non_blocking=True)
+    n_slot = int(lq[nblk > 0].sum())
+    positions, slots, cu_q, cu_k, ctx_lens = b200.step_metadata(seq_info, bt_dev, block_size, T, n_slot)
+    max_q = int(lq.max(initial=0))
+    ctx = Context(
+        is_prefill=max_q != 1,
+        cu_seqlens_q=cu_q,
+        cu_seqlens_k=cu_k,
+        max_seqlen_q=max_q,
+        max_seqlen_k=int(end.max(initial=0)),
+        slot_mapping=slots,
+        context_lens=ctx_lens,
+        block_tables=((bt_dev if width > 0 else torch.empty(B, 0, dtype=torch.int32, device=device))
+                      if attends_cache else None),
+    )
+    return ids_dev, positions, ctx

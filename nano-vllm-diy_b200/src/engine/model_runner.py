@@ -16,6 +16,8 @@ caller.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 
@@ -94,7 +96,13 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ steps
     def prepare(self, seqs) -> tuple[torch.Tensor, torch.Tensor, Context]:
-        return M.to_device(M.build(seqs, self.block_size), self.device)
+        """input_ids, positions and the Context of a step: per-sequence values
+        from the host, the per-token expansion on the device
+        (b200_step_metadata); B200_HOST_METADATA=1 builds everything on the
+        host instead."""
+        if os.environ.get("B200_HOST_METADATA") == "1":
+            return M.to_device(M.build(seqs, self.block_size), self.device)
+        return M.build_on_device(seqs, self.block_size, self.device)
 
     @torch.inference_mode()
     def run_hidden(self, input_ids: torch.Tensor, positions: torch.Tensor,

@@ -75,3 +75,55 @@ def test_decode_batch_properties():
                                        61 * 256 + 0, 83 * 256 + 999 % 256]
     assert m.block_tables is not None and m.block_tables.shape == (5, 4)
     assert m.block_tables[0].tolist() == [0, -1, -1, -1]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("seed", range(12))
+@pytest.mark.parametrize("block_size", [256, 512])
+def test_device_builder_matches_prepare_seqs(seed, block_size):
+    """The device-side expansion (b200_step_metadata) against the oracle's
+    restatement of prepare_seqs, bit-exact, warm-up batches included."""
+    from src.engine.metadata import build_on_device
+    rng = random.Random(seed)
+    seqs = _random_batch(rng, block_size, allow_warmup=(seed == 0))
+    ref = prepare_seqs(seqs, block_size)
+    ids, pos, ctx = build_on_device(seqs, block_size, torch.device("cuda", 0))
+    torch.cuda.synchronize()
+    assert torch.equal(ids.cpu(), ref["input_ids"])
+    assert torch.equal(pos.cpu(), ref["positions"])
+    assert torch.equal(ctx.cu_seqlens_q.cpu(), ref["cu_seqlens_q"])
+    assert torch.equal(ctx.cu_seqlens_k.cpu(), ref["cu_seqlens_k"])
+    assert torch.equal(ctx.context_lens.cpu(), ref["context_lens"])
+    assert torch.equal(ctx.slot_mapping.cpu(), ref["slot_mapping"])
+    assert ctx.max_seqlen_q == ref["max_seqlen_q"] and ctx.max_seqlen_k == ref["max_seqlen_k"]
+    assert ctx.is_prefill == ref["is_prefill"]
+    if ref["block_tables"] is None:
+        assert ctx.block_tables is None
+    else:
+        assert torch.equal(ctx.block_tables.cpu(), ref["block_tables"])
+    from src import b200
+    assert b200.device_error(clear=True) == 0
+
+
+@pytest.mark.gpu
+def test_device_builder_against_reference_goldens():
+    """The batches the reference's own prepare_seqs ran on (tests/golden/metadata.pt)."""
+    from src.engine.metadata import build_on_device
+    import os
+    batches = torch.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "metadata.pt"))
+    for batch in batches:
+        seqs = [SeqState(s["token_ids"], s["num_cached_tokens"], s["num_scheduled_tokens"],
+                         s["block_table"]) for s in batch["seqs"]]
+        ids, pos, ctx = build_on_device(seqs, 256, torch.device("cuda", 0))
+        torch.cuda.synchronize()
+        got = {"input_ids": ids, "positions": pos, "cu_seqlens_q": ctx.cu_seqlens_q,
+               "cu_seqlens_k": ctx.cu_seqlens_k, "context_lens": ctx.context_lens,
+               "slot_mapping": ctx.slot_mapping}
+        for key, t in got.items():
+            assert torch.equal(t.cpu(), batch[key].to(t.dtype)), key
+        if batch["block_tables"] is None:
+            assert ctx.block_tables is None
+        else:
+            assert torch.equal(ctx.block_tables.cpu(), batch["block_tables"])
+        assert ctx.max_seqlen_q == batch["max_seqlen_q"] and ctx.max_seqlen_k == batch["max_seqlen_k"]
+        assert ctx.is_prefill == batch["is_prefill"]
