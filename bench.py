@@ -514,10 +514,12 @@ def run_b200(args, rank: int, world: int):
 
 def run_microbench(args):
     """Kernel microbenchmarks (one JSON line each), used for ncu captures.
-      attn : BASELINE config 3 -- paged decode attention, B=256, ctx ~U[128,4096],
-             32 q / 8 kv heads, N(0,1) bf16, block 256, random block permutation,
-             seed 1 -- plus the slot_mapping scatter of 256 new tokens
-      gemm : the Qwen3-8B TP1 decode GEMMs at 256 tokens"""
+      attn    : BASELINE config 3 -- paged decode attention, B=256, ctx ~U[128,4096],
+                32 q / 8 kv heads, N(0,1) bf16, block 256, random block permutation,
+                seed 1 -- plus the slot_mapping scatter of 256 new tokens
+      gemm    : the Qwen3-8B TP1 decode GEMMs at 256 tokens
+      prefill : prefill attention, fresh varlen and chunked over paged prefixes,
+                FLOPs against the tensor peak"""
     from src import b200
     from src.layers.attention import attend
     from src.utils.context import Context
@@ -582,6 +584,51 @@ def run_microbench(args):
                               "bytes": byts, "gbs": byts / ms / 1e6, "frac": byts / ms / 1e6 / hbm,
                               "scatter_ms": ms_sc, "scatter_gbs": sc_bytes / ms_sc / 1e6,
                               "peak_gbs": hbm, "peak_source": kind}), flush=True)
+        elif args.workload == "prefill":
+            # Qwen3-8B heads (32 q / 8 kv, d 128): (a) fresh varlen prefill of 8
+            # prompts of 2048 tokens (per-token K / V); (b) chunked prefill: 16
+            # chunks of 512 tokens over 1536 cached tokens each (the scheduler's
+            # chunk size, src/engine/scheduler.py:90-98), K / V paged, block 256
+            Hq, Hkv = 32, 8
+            res = {}
+            gd = torch.Generator(device=dev).manual_seed(3)
+            scale = 128 ** -0.5
+            # (a) fresh
+            lens = [2048] * 8
+            cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=dev)
+            T = sum(lens)
+            q = torch.randn(T, Hq, 128, generator=gd, device=dev).to(torch.bfloat16)
+            k = torch.randn(T, Hkv, 128, generator=gd, device=dev).to(torch.bfloat16)
+            v = torch.randn(T, Hkv, 128, generator=gd, device=dev).to(torch.bfloat16)
+            pairs = sum(n * (n + 1) // 2 for n in lens)
+            ctx_a = Context(is_prefill=True, cu_seqlens_q=cu, cu_seqlens_k=cu, max_seqlen_q=2048,
+                            max_seqlen_k=2048)
+            out = torch.empty_like(q)
+            ms = timeit(lambda: attend(q, k, v, None, None, ctx_a, scale, out=out))
+            fl = 4.0 * 128 * Hq * pairs
+            res["fresh_8x2048"] = {"ms": ms, "tflops": fl / ms / 1e9, "frac": fl / ms / 1e9 / tflops}
+            # (b) chunked over paged prefixes
+            B, chunk, cached = 16, 512, 1536
+            Lk = chunk + cached
+            pages = (Lk + BLOCK - 1) // BLOCK
+            nblk = B * pages + 1
+            perm = torch.randperm(nblk, generator=torch.Generator().manual_seed(5))
+            bt = perm[:B * pages].view(B, pages).to(torch.int32).to(dev)
+            kc = torch.randn(nblk, BLOCK, Hkv, 128, generator=gd, device=dev).to(torch.bfloat16)
+            vc = torch.randn(nblk, BLOCK, Hkv, 128, generator=gd, device=dev).to(torch.bfloat16)
+            cu_q = torch.arange(0, (B + 1) * chunk, chunk, dtype=torch.int32, device=dev)
+            cu_k = torch.arange(0, (B + 1) * Lk, Lk, dtype=torch.int32, device=dev)
+            q2 = torch.randn(B * chunk, Hq, 128, generator=gd, device=dev).to(torch.bfloat16)
+            ctx_b = Context(is_prefill=True, cu_seqlens_q=cu_q, cu_seqlens_k=cu_k, max_seqlen_q=chunk,
+                            max_seqlen_k=Lk, block_tables=bt)
+            out2 = torch.empty_like(q2)
+            ms = timeit(lambda: attend(q2, None, None, kc, vc, ctx_b, scale, out=out2))
+            pairs = B * (chunk * cached + chunk * (chunk + 1) // 2)
+            fl = 4.0 * 128 * Hq * pairs
+            res["chunked_16x512_over_1536"] = {"ms": ms, "tflops": fl / ms / 1e9, "frac": fl / ms / 1e9 / tflops}
+            print(json.dumps({"workload": "prefill-attention (Qwen3-8B heads)",
+                              "kernel": os.environ.get("B200_PREFILL") or "tcgen05", "kernels": res,
+                              "tensor_peak_tflops": tflops, "peak_source": kind}), flush=True)
         else:
             T = 256
             shapes = {"qkv": (6144, 4096), "o_proj": (4096, 4096), "gate_up": (24576, 4096),
@@ -714,8 +761,8 @@ def main():
     ap.add_argument("--no-fused-ar", dest="fused_ar", action="store_false")
     ap.add_argument("--ar-mode", default="auto", choices=["auto", "oneshot", "twoshot"],
                     help="fused all-reduce exchange (allreduce workload)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attn", "gemm", "allreduce"],
-                    help="decode = the headline line; attn / gemm = kernel microbenchmarks")
+    ap.add_argument("--workload", default="decode", choices=["decode", "attn", "gemm", "allreduce", "prefill"],
+                    help="decode = the headline line; attn / gemm / prefill / allreduce = kernel microbenchmarks")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload == "decode":
         ap.error("--warmup must be >= 3")

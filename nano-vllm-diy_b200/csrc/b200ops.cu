@@ -22,6 +22,7 @@
 #include "elementwise.cuh"
 #include "exchange.cuh"
 #include "metadata.cuh"
+#include "prefill_tc.cuh"
 #include "gemm.cuh"
 #include "gemm_pair.cuh"
 #include "../../include/b200ops.h"
@@ -1202,6 +1203,41 @@ int b200_paged_attention(const void* q, long long q_stride, int num_q_rows, cons
     if (int r = ensure_smem(ds, 2u, decode_attn_kernel, smem)) return r;
     if (int r = launch_decode(ds, tmK, tmV, tmQ, a, smem, st)) return r;
     return check_launch("decode_attn_kernel");
+  }
+  // prefill on the tensor cores (tcgen05): 128-key tiles must not straddle
+  // pages; B200_PREFILL=legacy selects the mma.sync kernel below
+  const char* pf = getenv("B200_PREFILL");
+  const bool legacy = pf && std::strcmp(pf, "legacy") == 0;
+  if (!legacy && (!block_tables || page % kPtBN == 0) && num_q_rows > 0) {
+    CUtensorMap tmQ, tmK, tmV;
+    int r = make_tmap_3d(&tmQ, q, 128, Hq, (uint64_t)num_q_rows, 256, (uint64_t)q_stride * 2, 64, 1, kPtBM);
+    if (!r) {
+      if (block_tables) {
+        r = make_tmap_3d(&tmK, k_cache, 128, Hkv, (uint64_t)num_slots, 256, (uint64_t)Hkv * 256, 64, 1, kPtBN);
+        if (!r)
+          r = make_tmap_3d(&tmV, v_cache, 128, Hkv, (uint64_t)num_slots, 256, (uint64_t)Hkv * 256, 64, 1, kPtBN);
+      } else {
+        // without a block table K / V are per token, num_q_rows rows (the
+        // reference's fresh prefill: cu_seqlens_k == cu_seqlens_q)
+        r = make_tmap_3d(&tmK, k, 128, Hkv, (uint64_t)num_q_rows, 256, (uint64_t)k_stride * 2, 64, 1, kPtBN);
+        if (!r) r = make_tmap_3d(&tmV, v, 128, Hkv, (uint64_t)num_q_rows, 256, (uint64_t)v_stride * 2, 64, 1, kPtBN);
+      }
+    }
+    if (r) return r;
+    PrefillTcArgs t{};
+    t.cu_q = cu_seqlens_q; t.cu_k = cu_seqlens_k;
+    t.block_tables = block_tables; t.bt_stride = bt_stride; t.bt_width = bt_width;
+    t.num_slots = num_slots;
+    t.B = B; t.Hq = Hq; t.Hkv = Hkv; t.G = G; t.page = page > 0 ? page : 1;
+    t.scale_log2 = scale_log2;
+    t.out = static_cast<__nv_bfloat16*>(out); t.out_stride = out_stride;
+    t.err = ds->err;
+    if (int rr = ensure_smem(ds, 16u, prefill_tc_kernel, kPtSmemBytes)) return rr;
+    dim3 grid((max_seqlen_q + kPtBM - 1) / kPtBM, Hq, B);
+    const cudaError_t e = launch_ex(prefill_tc_kernel, grid, dim3(kPtThreads), kPtSmemBytes, st, nullptr, 0,
+                                    tmQ, tmK, tmV, t);
+    if (e != cudaSuccess) return fail(B200_ERR_CUDA, "prefill_tc launch: %s", cudaGetErrorString(e));
+    return check_launch("prefill_tc_kernel");
   }
   PrefillArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q); a.q_stride = q_stride;

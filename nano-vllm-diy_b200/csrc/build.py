@@ -16,7 +16,7 @@ LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libb200ops.so")
 SOURCES = ["b200ops.cu"]
 HEADERS = ["common.cuh", "gemm.cuh", "gemm_pair.cuh", "attention.cuh", "decode_attention.cuh",
-           "elementwise.cuh", "exchange.cuh", "metadata.cuh"]
+           "elementwise.cuh", "exchange.cuh", "metadata.cuh", "prefill_tc.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 

@@ -421,3 +421,50 @@ def test_prefill_attention_paged_prefix_and_chunks():
                                cu_k.to(DEV), max(lens_q), max(lens_k), scale, bt.to(DEV))
     torch.cuda.synchronize()
     assert L.rel_err(out.cpu(), ref) <= 2e-2
+
+
+@pytest.mark.parametrize("kernel", ["tcgen05", "legacy"])
+@pytest.mark.parametrize("Hq,Hkv,page", [(32, 8, 256), (16, 8, 512), (8, 1, 256), (4, 4, 256)])
+def test_prefill_attention_kernels_paged_with_stale_pages(kernel, Hq, Hkv, page, monkeypatch):
+    """Both prefill kernels (tcgen05 / TMEM / TMA, and the mma.sync one
+    selected by B200_PREFILL=legacy) on chunks, prefix hits, fresh prompts and
+    decode rows, with the unused tail of every last page holding NaN (stale
+    cache bits that P = 0 must not turn into NaN outputs)."""
+    from src import b200
+    monkeypatch.setenv("B200_PREFILL", "legacy" if kernel == "legacy" else "")
+    lens_q = [128, 1, 300, 129, 700, 1, 64]
+    lens_k = [128, 513, 300, 1000, 1400, 2, 2000]
+    q, kc, vc, bt, cu_q, cu_k = _paged_case(lens_q, lens_k, Hq, Hkv, page=page, seed=43)
+    for b, lk in enumerate(lens_k):
+        last = int(bt[b, (lk - 1) // page])
+        used = lk - ((lk - 1) // page) * page
+        kc[last, used:] = float("nan")
+        vc[last, used:] = float("nan")
+    scale = 128 ** -0.5
+    ref = L.varlen_attention(q, None, None, cu_q, cu_k, scale, kc, vc, bt)
+    out = b200.paged_attention(q.to(DEV), None, None, kc.to(DEV), vc.to(DEV), cu_q.to(DEV),
+                               cu_k.to(DEV), max(lens_q), max(lens_k), scale, bt.to(DEV))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert L.rel_err(out.cpu(), ref) <= 2e-2
+
+
+@pytest.mark.parametrize("kernel", ["tcgen05", "legacy"])
+def test_prefill_attention_kernels_fresh_long(kernel, monkeypatch):
+    """Fresh varlen prefill (per-token K / V), sequences up to 3000 tokens."""
+    from src import b200
+    monkeypatch.setenv("B200_PREFILL", "legacy" if kernel == "legacy" else "")
+    g = _g(44)
+    lens = [3000, 1, 127, 128, 129, 900]
+    Hq, Hkv = 16, 4
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32)
+    T = int(cu[-1])
+    q = torch.randn(T, Hq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(T, Hkv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, Hkv, 128, generator=g).to(torch.bfloat16)
+    scale = 128 ** -0.5
+    ref = L.varlen_attention(q, k, v, cu, cu, scale)
+    out = b200.paged_attention(q.to(DEV), k.to(DEV), v.to(DEV), None, None, cu.to(DEV), cu.to(DEV),
+                               max(lens), max(lens), scale, None)
+    torch.cuda.synchronize()
+    assert L.rel_err(out.cpu(), ref) <= 2e-2
