@@ -634,6 +634,8 @@ def run_microbench(args):
             shapes = {"qkv": (6144, 4096), "o_proj": (4096, 4096), "gate_up": (24576, 4096),
                       "down": (4096, 12288), "lm_head": (151936, 4096)}
             res = {}
+            if args.gemm_shapes:
+                shapes = {k: v for k, v in shapes.items() if k in args.gemm_shapes.split(",")}
             for name, (N, K) in shapes.items():
                 x = torch.randn(T, K, device=dev).to(torch.bfloat16)
                 # enough weight copies that consecutive calls stream from HBM
@@ -759,6 +761,8 @@ def main():
     ap.add_argument("--cpu-max-steps", type=int, default=3,
                     help="reference arm: timed CPU steps at most (each takes tens of seconds)")
     ap.add_argument("--no-fused-ar", dest="fused_ar", action="store_false")
+    ap.add_argument("--gemm-shapes", default="",
+                    help="gemm workload: comma list of qkv,o_proj,gate_up,down,lm_head (default all)")
     ap.add_argument("--ar-mode", default="auto", choices=["auto", "oneshot", "twoshot"],
                     help="fused all-reduce exchange (allreduce workload)")
     ap.add_argument("--workload", default="decode", choices=["decode", "attn", "gemm", "allreduce", "prefill"],
