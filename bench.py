@@ -82,7 +82,7 @@ def qwen3_8b_config():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -101,7 +101,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -367,19 +367,21 @@ def run_b200(args, rank: int, world: int):
         return float(t.item())
 
     stream = torch.cuda.current_stream()
+    # clocks are sampled over the whole loaded window (warm-up, the timed steps
+    # and the e2e steps below): the timed region alone is a few tenths of a
+    # second, a handful of samples
+    clocks = ClockSampler(dev).__enter__()
     for s in range(args.warmup):
         device_step(s)
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clocks:
-        ev0.record(stream)
-        for s in range(args.warmup, args.warmup + args.steps):
-            device_step(s)
-        ev1.record(stream)
-        barrier()
+    ev0.record(stream)
+    for s in range(args.warmup, args.warmup + args.steps):
+        device_step(s)
+    ev1.record(stream)
+    barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
     value = B / (ms / 1000.0)
-    clock_summary = clocks.summary()
 
     # ---- e2e: host metadata -> pinned H2D -> replay -> D2H tokens, per step
     h_lens = np.asarray(lens, dtype=np.int64)
@@ -425,6 +427,9 @@ def run_b200(args, rank: int, world: int):
     e1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    clocks.__exit__(None, None, None)
+    clock_summary = clocks.summary()
+    clock_summary["window"] = "warm-up, timed and e2e steps"
 
     # ---- roofline: decode attention of one layer, timed standalone
     hbm_peak, _, peak_kind = peaks()

@@ -50,7 +50,10 @@ int b200_version(void);
 unsigned long long b200_launch_count(void);
 
 /* Reads the device error word of the current device; clears it when `clear`
- * is non-zero.  Synchronous. */
+ * is non-zero.  Synchronous.  After a timeout bit (a bounded wait gave up),
+ * zero the first b200_attention_workspace_bytes(0, 0, 1) bytes of the
+ * attention workspace and the first 4096 bytes of the GEMM workspace before
+ * the next call: the kernel that gave up can leave counters behind. */
 int b200_device_error(unsigned* out, int clear);
 
 /* ------------------------------------------------------------------------

@@ -491,11 +491,9 @@ GemmPlan plan_pair_cluster(DeviceState* ds, int T, int N, int K, bool* resident,
       while (cols < np) cols <<= 1;
       p.tmem_cols = 2 * cols;
       // the ring receives ceil(NP/32 / C) chunks from each of the C - 1 others
-      // and stages the chunks this member sends
       const int nchunks = np / 32;
       const long long recv = (long long)((nchunks + c - 1) / c) * (c - 1) * kChunkFloats * 4;
-      const long long ring_need = (long long)(nchunks + ((nchunks + c - 1) / c) * (c - 2)) * kChunkFloats * 4;
-      if ((long long)p.stages * stage < ring_need) continue;
+      if ((long long)p.stages * stage < recv) continue;
       if ((*rc = ensure_smem(ds, 8u, gemm_pair_tcgen05_kernel, p.smem))) return GemmPlan{};
       const long long tiles = (long long)(p.n_tiles / 2) * token_tiles;
       const bool all_resident = tiles * 2 * c <= pair_resident(c, p.smem);

@@ -96,18 +96,6 @@ __device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, ui
       : "memory");
 }
 
-// Contiguous copy from this CTA's shared memory into another CTA's of the
-// cluster by the bulk-copy engine, completing `bytes` on that CTA's mbarrier
-// (both addresses 16-byte aligned, bytes a multiple of 16).
-__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
-                                                  uint32_t bar_cluster) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          dst_cluster),
-      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
-      : "memory");
-}
-
 // 2-D tiled store shared -> global by the TMA engine (clipped at the tensor
 // bounds), tracked by bulk async-groups.  c0 * element size must be a
 // multiple of 16 bytes and neither coordinate negative.
@@ -196,12 +184,11 @@ __device__ __forceinline__ long long sk_begin(long long total, int pr, int pairs
 // 2C CTAs = C pairs and one tile per cluster; member m = cluster rank / 2
 // computes K blocks [m nkb / C, (m + 1) nkb / C).  Member m owns the 32-wide
 // output chunks c with c % C == m.  After a cluster barrier (every ring of the
-// cluster is idle) each CTA sends the chunks other members own, staged from
-// TMEM in its own idle ring, into the owner's ring with bulk copies (counted
-// on the owner's mbarrier; slot (c / C) (C - 1) + the sender's index among
-// the owner's peers), then sums its own chunks from TMEM and the received
-// partials (members in rank order) and writes them: no L2 round trip and no
-// flags.
+// cluster is idle) each CTA pushes the chunks other members own from TMEM
+// straight into the owner's stage ring (st.async, counted on the owner's
+// mbarrier; slot (c / C) (C - 1) + the sender's index among the owner's
+// peers), then sums its own chunks from TMEM and the pushed partials (members
+// in rank order) and writes them: no L2 round trip and no flags.
 // ---------------------------------------------------------------------------
 
 // One segment of a pair's work: K blocks [kbb, kbe) of `tile`; `member` is
@@ -521,49 +508,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     };
     if (csk) {
       // ---- cluster split-K (see the schedule notes above).  The other
-      // members send their partials of this CTA's output chunks (c % C ==
-      // cmem) into ring slots [0, n_in): arm the byte count first.
+      // members push their partials of this CTA's output chunks (c % C ==
+      // cmem) into its ring: arm the byte count before the barrier.
       const int n_own = cmem < nchunks ? (nchunks - cmem + C - 1) / C : 0;
-      const int n_in = n_own * (C - 1);
-      if (lead_thread) mbar_arrive_expect_tx(&fix_bar[0], (uint32_t)n_in * kChunkFloats * 4);
+      if (lead_thread) mbar_arrive_expect_tx(&fix_bar[0], (uint32_t)(n_own * (C - 1)) * kChunkFloats * 4);
       const bool have = mbar_wait(&acc_full[0], 0u, p.err);
-      tc_fence_after();
-      const uint32_t d = tmem_base + ((uint32_t)(q * 32) << 16);
-      // the chunks other members own -> this CTA's own ring, slots n_in.. (its
-      // MMAs are done, so its ring is idle; the members' partials land in
-      // slots below n_in only after the cluster barrier)
-      {
-        int t = 0;
-        for (int c = 0; c < nchunks; ++c) {
-          if (c % C == cmem) continue;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(d + (uint32_t)(c * 32), r);
-          tmem_ld_wait_regs(r);
-          float4* dst = reinterpret_cast<float4*>(smem + (size_t)(n_in + t) * kChunkFloats * 4) + row;
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j * kGemmBM] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                           __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          ++t;
-        }
-      }
-      fence_proxy_async_smem();
       tc_fence_before();
       cluster_arrive();
-      cluster_wait();  // every pair of the cluster has finished its MMAs and staged its partials
+      cluster_wait();  // every pair of the cluster has finished its MMAs: every ring is idle
       tc_fence_after();
-      if (lead_thread) {
-        // one bulk copy per staged chunk into its owner's ring
-        int t = 0;
-        for (int c = 0; c < nchunks; ++c) {
-          if (c % C == cmem) continue;
+      const uint32_t d = tmem_base + ((uint32_t)(q * 32) << 16);
+      const uint32_t my_ring = smem_u32(smem) + (uint32_t)row * 16u;
+      const uint32_t my_bar = smem_u32(&fix_bar[0]);
+      // push the chunks owned by the other members, the next TMEM load
+      // overlapping this chunk's remote stores
+      auto next_push = [&](int c) {
+        do {
+          ++c;
+        } while (c < nchunks && c % C == cmem);
+        return c;
+      };
+      {
+        uint32_t rc[32], rn[32];
+        int c = next_push(-1);
+        if (c < nchunks) {
+          tmem_ld_32x32b_x32(d + (uint32_t)(c * 32), rc);
+          tmem_ld_wait_regs(rc);
+        }
+        while (c < nchunks) {
+          const int nx = next_push(c);
+          if (nx < nchunks) tmem_ld_32x32b_x32(d + (uint32_t)(nx * 32), rn);
           const int owner = c % C;
           const uint32_t peer = (uint32_t)(owner * 2) + v;  // the owner, same token half
           const int slot = (c / C) * (C - 1) + (cmem < owner ? cmem : cmem - 1);
-          bulk_copy_to_peer(map_to_rank(smem_u32(smem) + (uint32_t)slot * (uint32_t)(kChunkFloats * 4), peer),
-                            smem_u32(smem) + (uint32_t)(n_in + t) * (uint32_t)(kChunkFloats * 4),
-                            (uint32_t)(kChunkFloats * 4), map_to_rank(smem_u32(&fix_bar[0]), peer));
-          ++t;
+          const uint32_t dst = map_to_rank(my_ring, peer) + (uint32_t)slot * (uint32_t)(kChunkFloats * 4);
+          const uint32_t bar = map_to_rank(my_bar, peer);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            st_async_v4(dst + (uint32_t)(j * kGemmBM * 16), rc[4 * j], rc[4 * j + 1], rc[4 * j + 2],
+                        rc[4 * j + 3], bar);
+          if (nx < nchunks) tmem_ld_wait_regs(rn);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) rc[j] = rn[j];
+          c = nx;
         }
       }
       const bool got = mbar_wait_cluster(&fix_bar[0], 0u, p.err);
