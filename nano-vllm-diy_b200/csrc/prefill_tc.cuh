@@ -19,8 +19,10 @@
 //                 O  += P_j V_j   M = 128, N = 128 dims, K = 128 keys; P from
 //                                 shared memory (K-major), V MN-major (the
 //                                 cache's [key][dim] rows as they land)
-//   warps 2..5  softmax, one thread per query row (its TMEM lane): masked row
-//               maximum from S, then (once O += P_{j-1} V_{j-1} is done) the
+//   warps 2..9  softmax, two threads per query row (its TMEM lane): warps
+//               2-5 take key columns 0-63 of S (and dims 0-63 of O), warps 6-9
+//               columns 64-127; masked row maximum (halves combined through
+//               shared memory), then (once O += P_{j-1} V_{j-1} is done) the
 //               rescale of O in TMEM when the maximum grew, P = exp2(S * scale
 //               * log2 e - m) rounded to bf16 into shared memory (the operand
 //               rounding of flash attention), running sums in fp32; at the end
@@ -34,13 +36,14 @@ namespace b200 {
 
 constexpr int kPtBM = 128;       // queries per CTA
 constexpr int kPtBN = 128;       // keys per tile
-constexpr int kPtThreads = 192;
+constexpr int kPtThreads = 320;  // producer, MMA issuer, 8 softmax warps
 // shared memory (1024-byte aligned): Q | 2 x (K | V) | P | barriers
 constexpr int kPtQ = 0;
 constexpr int kPtStage = 32768;  // stage s: K at kPtStage + s * 65536, V 32 KB after it
 constexpr int kPtP = kPtStage + 2 * 65536;
 constexpr int kPtBar = kPtP + 32768;
-constexpr int kPtSmemBytes = 1024 + kPtBar + 128;
+constexpr int kPtRed = kPtBar + 128;  // float [2 halves][128 rows]: row maxima, then row sums
+constexpr int kPtSmemBytes = 1024 + kPtRed + 1024;
 
 struct PrefillTcArgs {
   const int* cu_q;
@@ -81,7 +84,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
   return d;
 }
 
-__device__ __forceinline__ void pt_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void pt_bar_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // The first cache row of key tile `key0` of sequence b (paged), or -1 when
 // the block table has no valid block for it.
@@ -216,17 +219,21 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       mbar_wait(mma_drain, 0u, a.err);
     }
   } else {
-    // ---- softmax / correction / epilogue: thread = query row (TMEM lane)
-    const int q = warp & 3;
+    // ---- softmax / correction / epilogue: two threads per query row (its
+    // TMEM lane), one per half of the columns
+    const int sw = warp - 2;           // 0..7
+    const int q = warp & 3;            // TMEM lane quarter of this warp
+    const int hf = sw >> 2;            // 0: S columns / O dims 0-63, 1: 64-127
     const int row = q * 32 + lane;
     const int i = i0 + row;            // query index inside the sequence
     const int vis = i + off;           // last key this row sees (inclusive)
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-    const bool lead = warp == 2 && lane == 0;
-    float m = -INFINITY, l = 0.f;
+    const bool lead = sw == 0 && lane == 0;
+    float* red = reinterpret_cast<float*>(smem + kPtRed);  // [2][128]
+    float m = -INFINITY, l = 0.f;      // l: this half's share of the row sum
     bool ok = true;
     // A wait that runs out sets s_abort; every softmax warp still reaches the
-    // named barrier of the iteration, and all of them leave the loop after it.
+    // named barriers of the iteration, and all of them leave the loop after it.
     for (int j = 0; j < ntiles; ++j) {
       const int s = j & 1;
       bool fail = !mbar_wait(&s_full[s], (uint32_t)(j >> 1) & 1u, a.err);
@@ -234,18 +241,29 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       const int key0 = j * kPtBN;
       const bool tile_ok = !paged || pt_tile_row(a, b, key0) >= 0;
       const int lim = tile_ok ? min(Lk - 1, vis) - key0 : -1;  // last valid key of the tile, local index
-      const uint32_t sa = tmem_base + lane_addr + 128u + (uint32_t)s * 128u;
-      // pass 1: masked row maximum (log2 domain)
+      // every row of the CTA sees the whole tile: no masking
+      const bool whole = tile_ok && key0 + kPtBN - 1 <= min(Lk - 1, i0 + off);
+      const uint32_t sa = tmem_base + lane_addr + 128u + (uint32_t)s * 128u + (uint32_t)(hf * 64);
+      // pass 1: masked maximum of this half (log2 domain), then the row's
       float mt = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(sa + (uint32_t)(c * 32), r);
         tmem_ld_wait();
+        const int col0 = hf * 64 + c * 32;
+        if (whole) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t)
-          if (c * 32 + t <= lim) mt = fmaxf(mt, __uint_as_float(r[t]) * a.scale_log2);
+          for (int t = 0; t < 32; ++t) mt = fmaxf(mt, __uint_as_float(r[t]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t) mt = fmaxf(mt, col0 + t <= lim ? __uint_as_float(r[t]) : -INFINITY);
+        }
       }
+      mt *= a.scale_log2;  // the scale is positive: max commutes with it
+      red[hf * 128 + row] = mt;
+      pt_bar_sync();
+      mt = fmaxf(red[row], red[128 + row]);
       const float m_new = fmaxf(m, mt);
       const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
       // O += P_{j-1} V_{j-1} must be done before P is rewritten or O rescaled
@@ -254,54 +272,57 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t oa = tmem_base + lane_addr + (uint32_t)(hf * 64 + c * 32);
             uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem_base + lane_addr + (uint32_t)(c * 32), r);
+            tmem_ld_32x32b_x32(oa, r);
             tmem_ld_wait();
 #pragma unroll
             for (int t = 0; t < 32; ++t) r[t] = __float_as_uint(__uint_as_float(r[t]) * alpha);
-            tmem_st_32x32b_x32(tmem_base + lane_addr + (uint32_t)(c * 32), r);
+            tmem_st_32x32b_x32(oa, r);
           }
           tmem_st_wait();
         }
       }
-      // pass 2: P = exp2(S' - m) as bf16 into the K-major, 128-byte swizzled
-      // P tile ([2 key halves][128 rows][128 B]); fp32 row sum
+      // pass 2: P = exp2(S' - m) as bf16 into this half's region of the
+      // K-major, 128-byte swizzled P tile ([2 key halves][128 rows][128 B])
       float rs = 0.f;
-      uint8_t* prow = smem + kPtP + row * 128;
+      uint8_t* prow = smem + kPtP + hf * 16384 + row * 128;
+      const bool live = m_new != -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(sa + (uint32_t)(c * 32), r);
         tmem_ld_wait();
+        const int col0 = hf * 64 + c * 32;
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const bool v0 = c * 32 + t <= lim, v1 = c * 32 + t + 1 <= lim;
-          const float p0 = (v0 && m_new != -INFINITY) ? fast_exp2(__uint_as_float(r[t]) * a.scale_log2 - m_new) : 0.f;
-          const float p1 = (v1 && m_new != -INFINITY) ? fast_exp2(__uint_as_float(r[t + 1]) * a.scale_log2 - m_new) : 0.f;
+          float p0 = fast_exp2(__uint_as_float(r[t]) * a.scale_log2 - m_new);
+          float p1 = fast_exp2(__uint_as_float(r[t + 1]) * a.scale_log2 - m_new);
+          if (!whole) {
+            p0 = (col0 + t <= lim && live) ? p0 : 0.f;
+            p1 = (col0 + t + 1 <= lim && live) ? p1 : 0.f;
+          }
           rs += p0 + p1;
           pk[t >> 1] = pack_bf16x2(p0, p1);
         }
-        uint8_t* half = prow + (c >> 1) * 16384;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int chunk = ((c & 1) * 4 + u) ^ (row & 7);
-          *reinterpret_cast<uint4*>(half + chunk * 16) =
+          const int chunk = (c * 4 + u) ^ (row & 7);
+          *reinterpret_cast<uint4*>(prow + chunk * 16) =
               make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
       }
       l = l * alpha + rs;
       m = m_new;
       // keys past the sequence (or a whole tile without a valid block) may hold
-      // stale cache bits: zero those V rows (P is 0 there, and 0 * NaN = NaN)
+      // stale cache bits: zero those V rows (P is 0 there, and 0 * NaN = NaN);
+      // each half zeroes its 64 dims
       if (paged && (!tile_ok || key0 + row >= Lk)) {
-        uint8_t* v = smem + kPtStage + s * 65536 + 32768 + row * 128;
+        uint8_t* v = smem + kPtStage + s * 65536 + 32768 + hf * 16384 + row * 128;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          *reinterpret_cast<uint4*>(v + u * 16) = make_uint4(0u, 0u, 0u, 0u);
-          *reinterpret_cast<uint4*>(v + 16384 + u * 16) = make_uint4(0u, 0u, 0u, 0u);
-        }
+        for (int u = 0; u < 8; ++u) *reinterpret_cast<uint4*>(v + u * 16) = make_uint4(0u, 0u, 0u, 0u);
       }
       if (fail) *s_abort = 1;
       fence_proxy_async_smem();
@@ -317,21 +338,24 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         mbar_arrive(p_full);
       }
     }
-    // ---- epilogue: O / l -> bf16 rows of this query head
+    // ---- epilogue: O / l -> bf16 rows of this query head, each half its dims
+    red[hf * 128 + row] = l;
+    pt_bar_sync();
+    const float lt = red[row] + red[128 + row];
     bool have = ntiles > 0 && ok;
     if (have) {
       have = mbar_wait(o_done, (uint32_t)(ntiles - 1) & 1u, a.err);
       tc_fence_after();
     }
-    const float f = have && l > 0.f ? 1.f / l : 0.f;
-    __nv_bfloat16* dst = a.out + (size_t)(q0 + i) * a.out_stride + (size_t)hq * 128;
+    const float f = have && lt > 0.f ? 1.f / lt : 0.f;
+    __nv_bfloat16* dst = a.out + (size_t)(q0 + i) * a.out_stride + (size_t)hq * 128 + hf * 64;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       uint32_t r[32];
 #pragma unroll
       for (int t = 0; t < 32; ++t) r[t] = 0u;
       if (ntiles > 0) {
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + (uint32_t)(c * 32), r);
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + (uint32_t)(hf * 64 + c * 32), r);
         tmem_ld_wait();
       }
       if (i < Lq) {
