@@ -64,12 +64,15 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Programmatic dependent launch of the kernels of this library (each one
 // waits for its predecessor with griddepcontrol.wait before it reads its
-// inputs, a no-op under a plain launch).  Off unless B200_PDL=1: measured on
-// the Qwen3-8B decode step it gained nothing at tp 1 and cost 4.5 % at tp 2
-// (early-launched dependents take SM resources from the running kernel).
-bool pdl_enabled() {
+// inputs, a no-op under a plain launch).  Off unless B200_PDL=1 (every
+// kernel) or B200_PDL=gemm (the GEMM kernels only): measured on the Qwen3-8B
+// decode step, on every kernel it gained nothing at tp 1 and cost 4.5 % at
+// tp 2 (early-launched dependents take SM resources from the running kernel).
+bool pdl_enabled(bool gemm = false) {
   const char* e = getenv("B200_PDL");
-  return e && *e == '1';
+  if (!e) return false;
+  if (*e == '1') return true;
+  return gemm && std::strcmp(e, "gemm") == 0;
 }
 
 // cudaLaunchKernelEx with the given attributes plus programmatic stream
@@ -532,7 +535,7 @@ int launch_pair(const GemmPlan& p, const CUtensorMap& tmW, const CUtensorMap& tm
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cfg.numAttrs = pdl_enabled(true) ? 2 : 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_tcgen05_kernel, tmW, tmX, tmY, a);
   if (e != cudaSuccess) return fail(B200_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
   return check_launch(what);
@@ -660,7 +663,7 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
     attr[nattr].val.clusterDim.z = p.splits;
     ++nattr;
   }
-  if (pdl_enabled()) {
+  if (pdl_enabled(true)) {
     attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[nattr].val.programmaticStreamSerializationAllowed = 1;
     ++nattr;
@@ -790,7 +793,7 @@ int run_gemm_allreduce(const void* x, long long ldx, const void* w, long long ld
     attr[nattr].val.clusterDim.z = p.splits;
     ++nattr;
   }
-  if (pdl_enabled()) {
+  if (pdl_enabled(true)) {
     attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[nattr].val.programmaticStreamSerializationAllowed = 1;
     ++nattr;

@@ -25,6 +25,9 @@ SMALL_06B = Qwen3Shape(hidden=1024, layers=3, heads=16, kv_heads=8, head_dim=128
                        vocab=151936, tie=True, max_pos=8192)
 WIDE_8B = Qwen3Shape(hidden=4096, layers=1, heads=32, kv_heads=8, head_dim=128, inter=12288,
                      vocab=8192, max_pos=8192)
+# Qwen3-32B's layer shapes: K = 5120, 64 q heads per 8 kv heads (GQA 8), FFN 25600
+WIDE_32B = Qwen3Shape(hidden=5120, layers=1, heads=64, kv_heads=8, head_dim=128, inter=25600,
+                      vocab=8192, max_pos=8192)
 PAGE = 256
 
 
@@ -65,7 +68,8 @@ def _run_both(shape, W, runner, okv, seqs, cos_sin):
     return hidden, logits, ref_h, ref_logits
 
 
-@pytest.mark.parametrize("shape", [TINY, SMALL_06B, WIDE_8B], ids=["tiny", "0.6b-3L", "8b-1L"])
+@pytest.mark.parametrize("shape", [TINY, SMALL_06B, WIDE_8B, WIDE_32B],
+                         ids=["tiny", "0.6b-3L", "8b-1L", "32b-1L"])
 def test_prefill_then_paged_decode(shape):
     from src.layers.pos_embedding import _table_cpu
     W = random_weights(shape, seed=3)
@@ -128,6 +132,63 @@ def test_chunked_prefill_and_prefix_mix():
     torch.cuda.synchronize()
     assert L.rel_err(h.cpu(), rh) <= 2e-2
     assert L.rel_err(lg.cpu(), rl) <= 2e-2
+
+
+def test_shared_prefix_groups():
+    """configs[4]'s pattern at small scale: groups of sequences sharing a
+    512-token prefix (two 256-token blocks in every member's block table).
+    The first member prefills the prefix and its suffix; the others hit the
+    prefix cache (num_cached_tokens = 512, only the suffix scheduled) and read
+    the shared blocks; then decode steps through the shared pages."""
+    from src.layers.pos_embedding import _table_cpu
+    shape = TINY
+    W = random_weights(shape, seed=15)
+    g = torch.Generator().manual_seed(16)
+    runner = _runner(shape, W, num_blocks=24)
+    okv = OM.OracleKV(shape, 24, PAGE)
+    cos_sin = _table_cpu(shape.max_pos, shape.head_dim, float(shape.theta))
+    groups = []
+    nxt = 0
+    for _ in range(2):
+        prefix = torch.randint(0, 4096, (512,), generator=g).tolist()
+        shared = [nxt, nxt + 1]
+        nxt += 2
+        members = []
+        for m in range(3):
+            suffix = torch.randint(0, 4096, (int(torch.randint(20, 200, (1,), generator=g)),),
+                                   generator=g).tolist()
+            table = shared + [nxt]
+            nxt += 1
+            members.append(SeqState(token_ids=prefix + suffix, block_table=table))
+        groups.append(members)
+    # step 1: each group's first member prefills prefix + suffix
+    first = [grp[0] for grp in groups]
+    for s_ in first:
+        s_.num_cached_tokens, s_.num_scheduled_tokens = 0, len(s_.token_ids)
+    _run_both(shape, W, runner, okv, first, cos_sin)
+    # step 2: the other members hit the 512-token prefix
+    others = [s_ for grp in groups for s_ in grp[1:]]
+    for s_ in others:
+        s_.num_cached_tokens, s_.num_scheduled_tokens = 512, len(s_.token_ids) - 512
+    h, lg, rh, rl = _run_both(shape, W, runner, okv, others, cos_sin)
+    torch.cuda.synchronize()
+    assert L.rel_err(lg.cpu(), rl) <= 2e-2
+    # decode steps for every member, teacher-forced on the oracle
+    everyone = [s_ for grp in groups for s_ in grp]
+    toks = {id(s_): t for s_, t in zip(others, rl.float().argmax(-1).tolist())}
+    for s_ in first:
+        toks[id(s_)] = 7
+    for step in range(3):
+        for s_ in everyone:
+            s_.num_cached_tokens = len(s_.token_ids)
+            s_.token_ids.append(int(toks[id(s_)]))
+            s_.num_scheduled_tokens = 1
+        h, lg, rh, rl = _run_both(shape, W, runner, okv, everyone, cos_sin)
+        torch.cuda.synchronize()
+        assert L.rel_err(lg.cpu(), rl) <= 2e-2, step
+        toks = {id(s_): t for s_, t in zip(everyone, rl.float().argmax(-1).tolist())}
+    from src import b200
+    assert b200.device_error() == 0
 
 
 def test_cuda_graph_decode_matches_eager():
