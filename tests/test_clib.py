@@ -48,6 +48,26 @@ def test_invalid_arguments_fail_before_any_launch():
     rc = lib.b200_rms_norm(ctypes.c_void_p(16), 12, None, ctypes.c_void_p(16), ctypes.c_void_p(16),
                            12, None, 1, 12, 1e-6, None)
     assert rc == -2
+    # token selection: the vocabulary start must leave room for 32-bit indices
+    rc = lib.b200_select_tokens_partial(ctypes.c_void_p(16), 100, 2, 100, 1 << 33, None, None, 0,
+                                        0, 0, ctypes.c_void_p(16), None)
+    assert rc == -1
+    # the keys exchange needs the peers' key slots at world > 1, and rows <= max_rows
+    rc = lib.b200_select_tokens_exchange(ctypes.c_void_p(16), 4, 0, 2, None, None, None, 4,
+                                         ctypes.c_void_p(16), None)
+    assert rc == -1
+    # the embedding exchange needs 8-element rows
+    rc = lib.b200_embedding_exchange(ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 12, 0, 10, 10, 0, 1,
+                                     (ctypes.c_void_p * 1)(16), 12, None, None, None)
+    assert rc == -1
+    # step metadata: a block table needs a slot mapping output, pages are positive
+    rc = lib.b200_step_metadata(ctypes.c_void_p(16), None, 0, 4, 0, ctypes.c_void_p(16), None,
+                                ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), None)
+    assert rc == -1
+    # the fused all-reduce's plan query rejects a bad shape without a device call
+    ok = ctypes.c_int(7)
+    rc = lib.b200_linear_allreduce_supported(256, 4100, 4096, 2, 512, 4096, 4096, ctypes.byref(ok))
+    assert rc == -1 and ok.value == 0
 
 
 def test_gemm_schedule_partitions_the_work():
@@ -95,6 +115,11 @@ def test_every_python_op_refuses_cpu_tensors():
         lambda: b200.paged_attention(q, kv, kv, None, None, i32, i32, 1, 4, 0.1),
         lambda: b200.embedding(torch.zeros(4, dtype=torch.int64), w, 0, 128),
         lambda: b200.argmax(x),
+        lambda: b200.select_tokens(x),
+        lambda: b200.tokens_from_keys(torch.zeros(4, dtype=torch.int64)),
+        lambda: b200.embedding_exchange(torch.zeros(4, dtype=torch.int64), w, 0, 128, 128, 0, 1,
+                                        [0], 64, None, None),
+        lambda: b200.step_metadata(torch.zeros(3, 4, dtype=torch.int32), None, 256, 4, 0),
     ]
     for call in calls:
         with pytest.raises(RuntimeError, match="CUDA tensors"):
