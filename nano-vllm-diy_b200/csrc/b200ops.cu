@@ -237,6 +237,7 @@ int make_tmap_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uin
 // ---------------------------------------------------------------------------
 struct GemmPlan {
   int BN, token_tiles, n_tiles, num_kb, kb_per_split, splits, stages, smem, tmem_cols;
+  int kstep = 1;  // SM-pair kernel: 64-wide K blocks per ring stage
   // SM-pair kernel schedule (GemmArgs::sched, grp_*, csplit)
   int sched, grp_whole, grp_split, grp_size, csplit;
 };
@@ -422,13 +423,22 @@ size_t pair_workspace_bytes(int num_sms) { return 4096 + (size_t)num_sms * 256 *
 // 2 x feature tiles, TMEM = two accumulators of pow2(NP) columns.
 // `splits` holds the number of pairs launched (pair_schedule over the
 // co-resident pairs).
+// 64-wide K blocks per ring stage of the SM-pair kernel: 2 (one 32-64 KB
+// stage per two blocks, half the barrier round trips per byte; measured
+// faster TMA streaming with the same bytes in flight) unless B200_GEMM_KSTEP=1.
+int pair_kstep() {
+  const char* e = getenv("B200_GEMM_KSTEP");
+  return (e && *e == '1') ? 1 : 2;
+}
+
 GemmPlan plan_pair(DeviceState* ds, int T, int N, int K, bool silu_tiles, int* rc) {
   GemmPlan p{};
   p.BN = silu_tiles ? 256 : std::min(256, std::max(32, round_up(N, 32)));
   p.token_tiles = (T + 2 * kGemmBM - 1) / (2 * kGemmBM);
   p.n_tiles = 2 * (silu_tiles ? (N / 2 + 127) / 128 : (N + p.BN - 1) / p.BN);
   p.num_kb = (K + kGemmBK - 1) / kGemmBK;
-  const int stage = kGemmBM * kGemmBK * 2 + (p.BN / 2) * kGemmBK * 2;
+  p.kstep = pair_kstep();
+  const int stage = p.kstep * (kGemmBM * kGemmBK * 2 + (p.BN / 2) * kGemmBK * 2);
   const int extra = 4 * kGemmBM * 64 + 512;  // output staging + barriers
   p.stages = std::min(kGemmMaxStages, (kPairSmemBudget - 1024 - extra) / stage);
   p.smem = 1024 + p.stages * stage + extra;
@@ -486,7 +496,9 @@ GemmPlan plan_pair_cluster(DeviceState* ds, int T, int N, int K, bool* resident,
       p.token_tiles = token_tiles;
       p.n_tiles = 2 * ((N + np - 1) / np);
       p.num_kb = num_kb;
-      const int stage = kGemmBM * kGemmBK * 2 + (np / 2) * kGemmBK * 2;
+      p.kstep = pair_kstep();
+      const int blk = kGemmBM * kGemmBK * 2 + (np / 2) * kGemmBK * 2;  // one 64-wide K block
+      const int stage = p.kstep * blk;
       const int extra = 4 * kGemmBM * 64 + 512;
       p.stages = std::min(kGemmMaxStages, (kPairSmemBudget - 1024 - extra) / stage);
       p.smem = 1024 + p.stages * stage + extra;
@@ -505,7 +517,7 @@ GemmPlan plan_pair_cluster(DeviceState* ds, int T, int N, int K, bool* resident,
       p.csplit = c;
       p.splits = (int)(c * tiles);
       const double kb_share = (double)((num_kb + c - 1) / c);
-      const double cost = kb_share * (double)stage / 74e3 + (double)recv / 150e3 + 1.0;  // us
+      const double cost = kb_share * (double)blk / 74e3 + (double)recv / 150e3 + 1.0;  // us
       if (cost < best_cost) {
         best_cost = cost;
         best = p;
@@ -602,6 +614,7 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
     GemmArgs a{};
     a.T = T; a.N = N; a.K = K; a.BN = p.BN; a.stages = p.stages; a.num_kb = p.num_kb;
     a.kb_per_split = p.kb_per_split; a.splits = p.splits; a.tmem_cols = p.tmem_cols;
+    a.kstep = p.kstep;
     a.epi = silu ? EPI_SILU : EPI_BF16;
     a.vec_ok = aligned16(y) && (ldy % 8 == 0);
     a.y = static_cast<__nv_bfloat16*>(y); a.ldy = ldy;

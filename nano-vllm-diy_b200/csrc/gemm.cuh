@@ -91,6 +91,7 @@ struct GemmArgs {
   // grp_split + p + j * pairs
   int sched;
   int grp_whole, grp_split, grp_size;
+  int kstep;           // SM-pair kernel: 64-wide K blocks per ring stage (1 or 2)
   int csplit;          // 2: cluster split-K (clusters of 2 pairs, one tile each, K halves
                        // reduced through distributed shared memory); 0: off
   unsigned* err;
@@ -191,142 +192,135 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, SumFn& sum8, in
         for (int i = 0; i < 8 && feat + i < p.silu_inter; ++i) dst[i] = __float2bfloat16_rn(o[i]);
       }
     }
-  } else if (p.epi == EPI_ALLREDUCE && p.ar.oneshot) {
-    // ---- one-shot all-reduce: every rank pushes its bf16 partial of this CTA
-    // position into every rank's staging (peer stores), then sums the world's
-    // partials for its own copy.  Staging and flags alternate between two
-    // halves by call parity, read from a device-side call counter, so a rank
-    // that is already one call ahead never overwrites data still being read.
-    const AllReducePeers& ar = p.ar;
-    unsigned* calls = ar.done[ar.rank];
-    const unsigned parity = __ldcg(calls) & 1u;
-    const size_t half = (size_t)ar.world * ar.stage_rows * ar.ldo;
-    const int units = (te - tb) * 16;
-    for (int u = threadIdx.x; u < units; u += kGemmThreads) {
-      const int t = tb + (u >> 4), ch = u & 15;
-      const int n = n0 + ch * 8;
-      if (n >= p.N) continue;
-      float v[8];
-      sum8(t * kGemmBM + ch * 8, v);
-      if (p.bias != nullptr) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
-      }
-      uint4 pk;
-      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
-      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
-      const size_t off = parity * half + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n;
-      for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.stage[r] + off) = pk;
-    }
-    __syncthreads();
-    __shared__ int s_ok1;
-    if (threadIdx.x == 0) {
-      signal_peers(ar.flags, parity * ar.positions + pos, ar.rank, ar.world);
-      s_ok1 = ar.world == 1 ||
-              wait_flag_and_reset(ar.flags[ar.rank] + parity * ar.positions + pos,
-                                  (unsigned)(ar.world - 1), p.err);
-    }
-    __syncthreads();
-    if (s_ok1) {
-      for (int u = threadIdx.x; u < units; u += kGemmThreads) {
-        const int t = tb + (u >> 4), ch = u & 15;
-        const int n = n0 + ch * 8;
-        if (n >= p.N) continue;
-        float acc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
-          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
-              ar.stage[ar.rank] + parity * half + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = unpack_bf16x2(qw[k]);
-            acc[2 * k] += f.x;
-            acc[2 * k + 1] += f.y;
-          }
-        }
-        uint4 pk;
-        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
-        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4*>(ar.out[ar.rank] + (size_t)(t0 + t) * ar.ldo + n) = pk;
-      }
-    }
-    // the last CTA to finish advances the call counter (every rank runs the
-    // same calls, so the counters stay equal)
-    if (threadIdx.x == 0) {
-      __threadfence();
-      if (atomicAdd(calls + 1, 1u) == nctas - 1) {
-        atomicExch(calls + 1, 0u);
-        atomicAdd(calls, 1u);
-      }
-    }
   } else if (p.epi == EPI_ALLREDUCE) {
-    // ---- two-shot all-reduce over NVLink peer memory, spread evenly over
-    // the CTAs that share this position (same tile on every rank): the
-    // position's token rows are cut into `world` sub-slices; rank r's CTA
-    // reduces sub-slice r.  Phase 1: push sub-slice s of this rank's bf16
-    // partial to rank s.  Phase 2: when the world's partials of sub-slice
-    // `rank` are in, sum them (fixed rank order) and store the result into
-    // every rank's output.  Phase 3: wait until the other sub-slices have
-    // arrived here, so the kernel's completion means the output is complete.
+    // ---- all-reduce over NVLink peer memory.  One-shot: every rank pushes
+    // its bf16 partial of this CTA position into every rank's staging, then
+    // sums the world's partials for its own copy; staging and flags alternate
+    // between two halves by call parity (a device-side call counter), so a
+    // rank one call ahead never overwrites data still being read.  Two-shot:
+    // the position's token rows are cut into `world` sub-slices and rank r's
+    // CTA reduces sub-slice r: push sub-slice s of this rank's partial to
+    // rank s; when the world's partials of sub-slice `rank` are in, sum them
+    // and store the result into every rank's output; then wait until the
+    // other sub-slices have arrived here, so the kernel's completion means
+    // the output is complete.
+    // Both loops keep several loads in flight per thread (distributed shared
+    // memory for the split-K sum, L2 for the staged partials): one latency
+    // per batch instead of one per 8-feature unit.
     const AllReducePeers& ar = p.ar;
+    const bool one = ar.oneshot != 0;
+    unsigned* calls = ar.done[ar.rank];
+    const unsigned parity = one ? (__ldcg(calls) & 1u) : 0u;
+    const size_t half = one ? (size_t)ar.world * ar.stage_rows * ar.ldo : 0;
     const int rows = te - tb;
     const int sub = (rows + ar.world - 1) / ar.world;
-    for (int u = threadIdx.x; u < rows * 16; u += kGemmThreads) {
-      const int t = tb + (u >> 4), ch = u & 15;
-      const int n = n0 + ch * 8;
-      if (n >= p.N) continue;
-      float v[8];
-      sum8(t * kGemmBM + ch * 8, v);
-      if (p.bias != nullptr) {
+    const int units = rows * 16;
+    constexpr int kPushBatch = 4;
+    for (int ub = threadIdx.x; ub < units; ub += kPushBatch * kGemmThreads) {
+      uint4 pk[kPushBatch];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
-      }
-      uint4 pk;
-      pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
-      pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
-      const int dst = (t - tb) / sub;  // rank reducing this row
-      *reinterpret_cast<uint4*>(ar.stage[dst] + ((size_t)ar.rank * ar.stage_rows + t0 + t) * ar.ldo + n) = pk;
-    }
-    __syncthreads();
-    __shared__ int s_ok2;
-    if (threadIdx.x == 0) {
-      signal_peers(ar.flags, pos, ar.rank, ar.world);
-      s_ok2 = wait_flag_and_reset(ar.flags[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
-    }
-    __syncthreads();
-    const int mb = tb + ar.rank * sub, me = min(te, mb + sub);
-    if (s_ok2) {
-      for (int u = threadIdx.x; u < max(0, me - mb) * 16; u += kGemmThreads) {
-        const int t = mb + (u >> 4), ch = u & 15;
-        const int n = n0 + ch * 8;
+      for (int j = 0; j < kPushBatch; ++j) {
+        const int u = ub + j * kGemmThreads;
+        if (u >= units) break;
+        const int t = tb + (u >> 4), n = n0 + (u & 15) * 8;
         if (n >= p.N) continue;
-        float acc[8];
+        float v[8];
+        sum8(t * kGemmBM + (u & 15) * 8, v);
+        if (p.bias != nullptr) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int r = 0; r < ar.world; ++r) {  // fixed order: identical sums on every rank
-          const uint4 q = __ldcg(reinterpret_cast<const uint4*>(
-              ar.stage[ar.rank] + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
-          const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q);
+          for (int i = 0; i < 8; ++i)
+            if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+        }
+        pk[j].x = pack_bf16x2(v[0], v[1]); pk[j].y = pack_bf16x2(v[2], v[3]);
+        pk[j].z = pack_bf16x2(v[4], v[5]); pk[j].w = pack_bf16x2(v[6], v[7]);
+      }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = unpack_bf16x2(qw[k]);
-            acc[2 * k] += f.x;
-            acc[2 * k + 1] += f.y;
+      for (int j = 0; j < kPushBatch; ++j) {
+        const int u = ub + j * kGemmThreads;
+        if (u >= units) break;
+        const int t = tb + (u >> 4), n = n0 + (u & 15) * 8;
+        if (n >= p.N) continue;
+        const size_t row = (size_t)ar.rank * ar.stage_rows + t0 + t;
+        if (one) {
+          const size_t off = parity * half + row * ar.ldo + n;
+          for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.stage[r] + off) = pk[j];
+        } else {
+          *reinterpret_cast<uint4*>(ar.stage[(t - tb) / sub] + row * ar.ldo + n) = pk[j];
+        }
+      }
+    }
+    __syncthreads();
+    __shared__ int s_ok;
+    const size_t fbase = parity * (size_t)ar.positions;
+    if (threadIdx.x == 0) {
+      signal_peers(ar.flags, fbase + pos, ar.rank, ar.world);
+      s_ok = ar.world == 1 ||
+             wait_flag_and_reset(ar.flags[ar.rank] + fbase + pos, (unsigned)(ar.world - 1), p.err);
+    }
+    __syncthreads();
+    // rows this CTA reduces: all of them (one-shot) or sub-slice `rank`
+    const int mb = one ? tb : tb + ar.rank * sub;
+    const int me = one ? te : min(te, mb + sub);
+    const int units2 = max(0, me - mb) * 16;
+    // batches of G units x world partials, at most 8 loads of 16 bytes
+    const int G = max(1, 8 / ar.world);
+    if (s_ok) {
+      for (int ub = threadIdx.x; ub < units2; ub += G * kGemmThreads) {
+        uint4 q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int j = i / ar.world, r = i - j * ar.world;
+          const int u = ub + j * kGemmThreads;
+          if (j < G && u < units2) {
+            const int t = mb + (u >> 4), n = n0 + (u & 15) * 8;
+            if (n < p.N)
+              q[i] = __ldcg(reinterpret_cast<const uint4*>(
+                  ar.stage[ar.rank] + parity * half + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
           }
         }
-        uint4 pk;
-        pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
-        pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
-        for (int r = 0; r < ar.world; ++r)
-          *reinterpret_cast<uint4*>(ar.out[r] + (size_t)(t0 + t) * ar.ldo + n) = pk;
+        for (int j = 0; j < G; ++j) {
+          const int u = ub + j * kGemmThreads;
+          if (u >= units2) break;
+          const int t = mb + (u >> 4), n = n0 + (u & 15) * 8;
+          if (n >= p.N) continue;
+          float acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {  // slots in rank order: identical sums on every rank
+            if (i / ar.world != j) continue;
+            const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q[i]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = unpack_bf16x2(qw[k]);
+              acc[2 * k] += f.x;
+              acc[2 * k + 1] += f.y;
+            }
+          }
+          uint4 pk;
+          pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
+          pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
+          const size_t off = (size_t)(t0 + t) * ar.ldo + n;
+          if (one) {
+            *reinterpret_cast<uint4*>(ar.out[ar.rank] + off) = pk;
+          } else {
+            for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.out[r] + off) = pk;
+          }
+        }
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (one) {
+      // the last CTA to finish advances the call counter (every rank runs the
+      // same calls, so the counters stay equal)
+      if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(calls + 1, 1u) == nctas - 1) {
+          atomicExch(calls + 1, 0u);
+          atomicAdd(calls, 1u);
+        }
+      }
+    } else if (threadIdx.x == 0) {
       signal_peers(ar.done, pos, ar.rank, ar.world);
       wait_flag_and_reset(ar.done[ar.rank] + pos, (unsigned)(ar.world - 1), p.err);
     }

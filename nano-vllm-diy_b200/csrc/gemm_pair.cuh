@@ -262,12 +262,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr uint32_t kABytes = kGemmBM * kGemmBK * 2;  // 16 KiB: 128 tokens
   const int NP = p.BN;                                  // the pair's tile columns
   const uint32_t b_bytes = (uint32_t)(NP / 2) * kGemmBK * 2;
+  // a ring stage holds KS consecutive 64-wide K blocks (one TMA box per
+  // block and operand); the MMA issuer waits once per stage
+  const int KS = p.kstep >= 2 ? 2 : 1;
+  const uint32_t a_stage = (uint32_t)KS * kABytes, b_stage = (uint32_t)KS * b_bytes;
   uint8_t* a_smem = smem;
-  uint8_t* b_smem = smem + (size_t)S * kABytes;
+  uint8_t* b_smem = smem + (size_t)S * a_stage;
   // output staging for the TMA stores: 4 x [128 tokens][32 features] bf16,
   // 64-byte rows with the 64-byte swizzle (16-byte chunk c of row r at
   // chunk c ^ ((r >> 1) & 3)), 1 KiB aligned
-  uint8_t* stage_out = b_smem + (size_t)S * b_bytes;
+  uint8_t* stage_out = b_smem + (size_t)S * b_stage;
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_out + 4 * kGemmBM * 64);
   uint64_t* empty = full + kGemmMaxStages;
   uint64_t* acc_full = empty + kGemmMaxStages;   // [2] per CTA
@@ -367,11 +371,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         PairSeg s0;
         if (next_seg(su0, sk0, s0)) {
           const int wrow = weight_row(s0.tile);
-          pre = min(S, s0.kbe - s0.kbb);
+          pre = min(S, (s0.kbe - s0.kbb + KS - 1) / KS);
           for (int j = 0; j < pre; ++j) {
-            if (v == 0) mbar_arrive_expect_tx(&full[j], 2u * (kABytes + b_bytes));
-            tma_load_2d_pair(smem_u32(b_smem + (size_t)j * b_bytes), &tmW, full_leader + (uint32_t)j * 8u,
-                             (s0.kbb + j) * kGemmBK, wrow);
+            const int kb = s0.kbb + j * KS, nb = min(KS, s0.kbe - kb);
+            if (v == 0) mbar_arrive_expect_tx(&full[j], 2u * (uint32_t)nb * (kABytes + b_bytes));
+            for (int h = 0; h < nb; ++h)
+              tma_load_2d_pair(smem_u32(b_smem + (size_t)j * b_stage + (size_t)h * b_bytes), &tmW,
+                               full_leader + (uint32_t)j * 8u, (kb + h) * kGemmBK, wrow);
           }
         }
       }
@@ -383,23 +389,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int tt = (int)(sg.tile - (long long)mt * p.tiles_t);
         const int tok = tt * 2 * kGemmBM + (int)v * kGemmBM;
         const int wrow = weight_row(sg.tile);
-        for (int kb = kbb; kb < kbe; ++kb, ++it) {
+        for (int kb = kbb; kb < kbe; kb += KS, ++it) {
           const int s = it % S;
           const uint32_t ph = (uint32_t)(it / S) & 1u;
+          const int nb = min(KS, kbe - kb);
+          const uint32_t bar = full_leader + (uint32_t)s * 8u;
           if (it < pre) {  // weights already in flight: the activations now
-            tma_load_2d_pair(smem_u32(a_smem + (size_t)s * kABytes), &tmX, full_leader + (uint32_t)s * 8u,
-                             kb * kGemmBK, tok);
+            for (int h = 0; h < nb; ++h)
+              tma_load_2d_pair(smem_u32(a_smem + (size_t)s * a_stage + (size_t)h * kABytes), &tmX, bar,
+                               (kb + h) * kGemmBK, tok);
             continue;
           }
           if (!mbar_wait(&empty[s], ph ^ 1u, p.err)) {
             ok = false;
             break;
           }
-          if (v == 0) mbar_arrive_expect_tx(&full[s], 2u * (kABytes + b_bytes));
-          const int kc = kb * kGemmBK;
-          const uint32_t bar = full_leader + (uint32_t)s * 8u;
-          tma_load_2d_pair(smem_u32(a_smem + (size_t)s * kABytes), &tmX, bar, kc, tok);
-          tma_load_2d_pair(smem_u32(b_smem + (size_t)s * b_bytes), &tmW, bar, kc, wrow);
+          if (v == 0) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)nb * (kABytes + b_bytes));
+          for (int h = 0; h < nb; ++h) {
+            const int kc = (kb + h) * kGemmBK;
+            tma_load_2d_pair(smem_u32(a_smem + (size_t)s * a_stage + (size_t)h * kABytes), &tmX, bar, kc, tok);
+            tma_load_2d_pair(smem_u32(b_smem + (size_t)s * b_stage + (size_t)h * b_bytes), &tmW, bar, kc, wrow);
+          }
         }
       }
       if (!ok && v == 0) {
@@ -429,20 +439,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait(&acc_empty[b], (((uint32_t)seg >> 1) & 1u) ^ 1u, p.err)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)b * acc_stride;
-        for (int kb = kbb; kb < kbe; ++kb, ++it) {
+        for (int kb = kbb; kb < kbe; kb += KS, ++it) {
           const int s = it % S;
           const uint32_t ph = (uint32_t)(it / S) & 1u;
+          const int nb = min(KS, kbe - kb);
           if (!mbar_wait(&full[s], ph, p.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(a_smem + (size_t)s * kABytes);
-          const uint32_t b_base = smem_u32(b_smem + (size_t)s * b_bytes);
+          for (int h = 0; h < nb; ++h) {
+            const uint32_t a_base = smem_u32(a_smem + (size_t)s * a_stage + (size_t)h * kABytes);
+            const uint32_t b_base = smem_u32(b_smem + (size_t)s * b_stage + (size_t)h * b_bytes);
 #pragma unroll
-          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
-            tc_mma_f16_pair(d, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32),
-                            idesc, (kb != kbb || kk != 0) ? 1u : 0u);
+            for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+              tc_mma_f16_pair(d, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32),
+                              idesc, (kb != kbb || h != 0 || kk != 0) ? 1u : 0u);
+            }
           }
           tc_commit_pair(empty_own + (uint32_t)s * 8u);
           tc_commit_pair(empty_peer + (uint32_t)s * 8u);
@@ -675,7 +688,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int H = silu ? 2 : 1;
           const int n_own = (nout - me + g - 1) / g;
           const int copies = n_own * (g - 1) * H;
-          const int ring_slots = (int)(((size_t)S * (kABytes + b_bytes)) / (kChunkFloats * 4));
+          const int ring_slots = (int)(((size_t)S * (a_stage + b_stage)) / (kChunkFloats * 4));
           const bool burst = p.grp_whole == 0 && copies <= ring_slots && copies <= 32;
           if (burst && lead_thread && s_grp_ok) {
             fence_proxy_async_global();  // the acquired partials, then bulk reads of them
@@ -808,7 +821,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       float* my_part = p.sk_part + ((size_t)pr * 2 + v) * (size_t)NP * kGemmBM;
       const int ncontrib = last_contrib - pr;
       // finisher: contributor partials stream into the idle stage ring
-      const int ring_slots = min(kFixSlots, (int)(((size_t)S * (kABytes + b_bytes)) / (kChunkFloats * 4)));
+      const int ring_slots = min(kFixSlots, (int)(((size_t)S * (a_stage + b_stage)) / (kChunkFloats * 4)));
       const int copies = ncontrib * nchunks;
       auto issue_copy = [&](int k) {  // copy k: TMEM chunk chunk_at(k / ncontrib) of contributor pr+1 + k % ncontrib
         const int slot = k % ring_slots;
