@@ -157,6 +157,57 @@ __device__ __forceinline__ void silu_mul2(float& g0, float& g1, float u0, float 
   g1 = __fmul_rn(s1, u1);
 }
 
+// Rows one all-reduce epilogue thread advances by (16 threads span a row).
+constexpr int kArRowStep = kGemmThreads / 16;
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&v)[8]) {
+  uint4 pk;
+  pk.x = pack_bf16x2(v[0], v[1]); pk.y = pack_bf16x2(v[2], v[3]);
+  pk.z = pack_bf16x2(v[4], v[5]); pk.w = pack_bf16x2(v[6], v[7]);
+  return pk;
+}
+
+// The all-reduce's sum: for this thread's rows tr = r0, r0 + kArRowStep, ...
+// < rows2, the W staged partials at src + tr ldo + r rstride (r = rank,
+// ascending: the same fp32 sum on every rank) are added and `emit(tr, bf16
+// x 8)` stores the result.  The W loads of G rows are in flight together.
+template <int W, typename Emit>
+__device__ __forceinline__ void ar_reduce_rows(const __nv_bfloat16* src, size_t rstride, long long ldo,
+                                               int rows2, int r0, Emit& emit) {
+  constexpr int G = W >= 8 ? 1 : 8 / W;
+  for (int tr0 = r0; tr0 < rows2; tr0 += G * kArRowStep) {
+    uint4 q[G][W];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int tr = tr0 + j * kArRowStep;
+      if (tr < rows2) {
+        const __nv_bfloat16* s = src + (size_t)tr * ldo;
+#pragma unroll
+        for (int r = 0; r < W; ++r) q[j][r] = __ldcg(reinterpret_cast<const uint4*>(s + r * rstride));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+      const int tr = tr0 + j * kArRowStep;
+      if (tr >= rows2) break;
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+      for (int r = 0; r < W; ++r) {
+        const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q[j][r]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = unpack_bf16x2(qw[k]);
+          acc[2 * k] += f.x;
+          acc[2 * k + 1] += f.y;
+        }
+      }
+      emit(tr, pack_bf16x8(acc));
+    }
+  }
+}
+
 // Epilogue shared by the GEMM kernels: this CTA's token rows [tb, te) of
 // the tile at (token t0, feature n0 / SiLU tile ntile).  `sum8(off, v)`
 // returns the 8 fp32 accumulators at float offset `off` of the [token][128]
@@ -204,9 +255,10 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, SumFn& sum8, in
     // and store the result into every rank's output; then wait until the
     // other sub-slices have arrived here, so the kernel's completion means
     // the output is complete.
-    // Both loops keep several loads in flight per thread (distributed shared
-    // memory for the split-K sum, L2 for the staged partials): one latency
-    // per batch instead of one per 8-feature unit.
+    // Every thread keeps one 8-feature chunk (16 threads span the tile's 128
+    // features) and walks the rows kArRowStep apart, with its addresses and
+    // bias computed once: the epilogue runs on the CTA's 6 warps, and its
+    // instruction count more than its bytes sets its time.
     const AllReducePeers& ar = p.ar;
     const bool one = ar.oneshot != 0;
     unsigned* calls = ar.done[ar.rank];
@@ -214,38 +266,41 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, SumFn& sum8, in
     const size_t half = one ? (size_t)ar.world * ar.stage_rows * ar.ldo : 0;
     const int rows = te - tb;
     const int sub = (rows + ar.world - 1) / ar.world;
-    const int units = rows * 16;
+    const int ch = threadIdx.x & 15;
+    const int n = n0 + ch * 8;
+    const bool n_ok = n < p.N;
+    const int r0 = threadIdx.x >> 4;
+    float bias8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      bias8[i] = (p.bias != nullptr && n + i < p.N) ? __bfloat162float(p.bias[n + i]) : 0.f;
+    // phase 1: this rank's partial rows [tb, te) -> the staging of every rank
+    // (one-shot) or of the rank reducing the row (two-shot); the split-K sums
+    // of four rows are formed before their stores
+    const size_t off1 = parity * half + ((size_t)ar.rank * ar.stage_rows + t0 + tb) * ar.ldo + n;
     constexpr int kPushBatch = 4;
-    for (int ub = threadIdx.x; ub < units; ub += kPushBatch * kGemmThreads) {
+    for (int tr0 = r0; tr0 < rows; tr0 += kPushBatch * kArRowStep) {
       uint4 pk[kPushBatch];
 #pragma unroll
       for (int j = 0; j < kPushBatch; ++j) {
-        const int u = ub + j * kGemmThreads;
-        if (u >= units) break;
-        const int t = tb + (u >> 4), n = n0 + (u & 15) * 8;
-        if (n >= p.N) continue;
-        float v[8];
-        sum8(t * kGemmBM + (u & 15) * 8, v);
-        if (p.bias != nullptr) {
+        const int tr = tr0 + j * kArRowStep;
+        if (tr < rows && n_ok) {
+          float v[8];
+          sum8((tb + tr) * kGemmBM + ch * 8, v);
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (n + i < p.N) v[i] += __bfloat162float(p.bias[n + i]);
+          for (int i = 0; i < 8; ++i) v[i] += bias8[i];
+          pk[j] = pack_bf16x8(v);
         }
-        pk[j].x = pack_bf16x2(v[0], v[1]); pk[j].y = pack_bf16x2(v[2], v[3]);
-        pk[j].z = pack_bf16x2(v[4], v[5]); pk[j].w = pack_bf16x2(v[6], v[7]);
       }
 #pragma unroll
       for (int j = 0; j < kPushBatch; ++j) {
-        const int u = ub + j * kGemmThreads;
-        if (u >= units) break;
-        const int t = tb + (u >> 4), n = n0 + (u & 15) * 8;
-        if (n >= p.N) continue;
-        const size_t row = (size_t)ar.rank * ar.stage_rows + t0 + t;
+        const int tr = tr0 + j * kArRowStep;
+        if (tr >= rows || !n_ok) continue;
+        const size_t off = off1 + (size_t)tr * ar.ldo;
         if (one) {
-          const size_t off = parity * half + row * ar.ldo + n;
           for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.stage[r] + off) = pk[j];
         } else {
-          *reinterpret_cast<uint4*>(ar.stage[(t - tb) / sub] + row * ar.ldo + n) = pk[j];
+          *reinterpret_cast<uint4*>(ar.stage[tr / sub] + off) = pk[j];
         }
       }
     }
@@ -258,55 +313,32 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, SumFn& sum8, in
              wait_flag_and_reset(ar.flags[ar.rank] + fbase + pos, (unsigned)(ar.world - 1), p.err);
     }
     __syncthreads();
-    // rows this CTA reduces: all of them (one-shot) or sub-slice `rank`
+    // phase 2: the rows this CTA reduces -- all of them (one-shot) or
+    // sub-slice `rank` (two-shot) -- summed over the world in rank order
     const int mb = one ? tb : tb + ar.rank * sub;
     const int me = one ? te : min(te, mb + sub);
-    const int units2 = max(0, me - mb) * 16;
-    // batches of G units x world partials, at most 8 loads of 16 bytes
-    const int G = max(1, 8 / ar.world);
-    if (s_ok) {
-      for (int ub = threadIdx.x; ub < units2; ub += G * kGemmThreads) {
-        uint4 q[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int j = i / ar.world, r = i - j * ar.world;
-          const int u = ub + j * kGemmThreads;
-          if (j < G && u < units2) {
-            const int t = mb + (u >> 4), n = n0 + (u & 15) * 8;
-            if (n < p.N)
-              q[i] = __ldcg(reinterpret_cast<const uint4*>(
-                  ar.stage[ar.rank] + parity * half + ((size_t)r * ar.stage_rows + t0 + t) * ar.ldo + n));
-          }
-        }
-        for (int j = 0; j < G; ++j) {
-          const int u = ub + j * kGemmThreads;
-          if (u >= units2) break;
-          const int t = mb + (u >> 4), n = n0 + (u & 15) * 8;
-          if (n >= p.N) continue;
-          float acc[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {  // slots in rank order: identical sums on every rank
-            if (i / ar.world != j) continue;
-            const uint32_t* qw = reinterpret_cast<const uint32_t*>(&q[i]);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = unpack_bf16x2(qw[k]);
-              acc[2 * k] += f.x;
-              acc[2 * k + 1] += f.y;
-            }
-          }
-          uint4 pk;
-          pk.x = pack_bf16x2(acc[0], acc[1]); pk.y = pack_bf16x2(acc[2], acc[3]);
-          pk.z = pack_bf16x2(acc[4], acc[5]); pk.w = pack_bf16x2(acc[6], acc[7]);
-          const size_t off = (size_t)(t0 + t) * ar.ldo + n;
-          if (one) {
-            *reinterpret_cast<uint4*>(ar.out[ar.rank] + off) = pk;
-          } else {
-            for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.out[r] + off) = pk;
-          }
-        }
+    const int rows2 = max(0, me - mb);
+    const __nv_bfloat16* src2 = ar.stage[ar.rank] + parity * half + (size_t)(t0 + mb) * ar.ldo + n;
+    const size_t rstride = (size_t)ar.stage_rows * ar.ldo;
+    const size_t off2 = (size_t)(t0 + mb) * ar.ldo + n;
+    auto emit = [&](int tr, const uint4& pk) {
+      const size_t off = off2 + (size_t)tr * ar.ldo;
+      if (one) {
+        *reinterpret_cast<uint4*>(ar.out[ar.rank] + off) = pk;
+      } else {
+        for (int r = 0; r < ar.world; ++r) *reinterpret_cast<uint4*>(ar.out[r] + off) = pk;
+      }
+    };
+    if (s_ok && n_ok) {
+      switch (ar.world) {
+        case 1: ar_reduce_rows<1>(src2, rstride, ar.ldo, rows2, r0, emit); break;
+        case 2: ar_reduce_rows<2>(src2, rstride, ar.ldo, rows2, r0, emit); break;
+        case 3: ar_reduce_rows<3>(src2, rstride, ar.ldo, rows2, r0, emit); break;
+        case 4: ar_reduce_rows<4>(src2, rstride, ar.ldo, rows2, r0, emit); break;
+        case 5: ar_reduce_rows<5>(src2, rstride, ar.ldo, rows2, r0, emit); break;
+        case 6: ar_reduce_rows<6>(src2, rstride, ar.ldo, rows2, r0, emit); break;
+        case 7: ar_reduce_rows<7>(src2, rstride, ar.ldo, rows2, r0, emit); break;
+        default: ar_reduce_rows<8>(src2, rstride, ar.ldo, rows2, r0, emit); break;
       }
     }
     __syncthreads();
@@ -515,16 +547,36 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   const int tb = min(rows_valid, (int)rank * per);
   const int te = min(rows_valid, tb + per);
   const uint32_t tile_local = smem_u32(s_tile);
+  // the cluster ranks' tiles (splits <= 8), mapped once
+  uint32_t rank_tile[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+    rank_tile[r] = (r < splits && splits > 1) ? map_to_rank(tile_local, (uint32_t)r) : tile_local;
+  // 8 fp32 partials summed over the cluster ranks in rank order, the loads of
+  // four ranks in flight together
   auto sum8 = [&](int off_floats, float* v) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.f;
-    for (int r = 0; r < splits; ++r) {
-      const uint32_t base = splits > 1 ? map_to_rank(tile_local, (uint32_t)r) : tile_local;
-      const uint32_t a = base + (uint32_t)off_floats * 4u;
-      const float4 x0 = ld_dsmem_f4(a);
-      const float4 x1 = ld_dsmem_f4(a + 16);
-      v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
-      v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+#pragma unroll
+    for (int g = 0; g < 8; g += 4) {
+      if (g < splits) {
+        float4 x[8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          if (g + r < splits) {
+            const uint32_t a = rank_tile[g + r] + (uint32_t)off_floats * 4u;
+            x[2 * r] = ld_dsmem_f4(a);
+            x[2 * r + 1] = ld_dsmem_f4(a + 16);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          if (g + r < splits) {
+            v[0] += x[2 * r].x; v[1] += x[2 * r].y; v[2] += x[2 * r].z; v[3] += x[2 * r].w;
+            v[4] += x[2 * r + 1].x; v[5] += x[2 * r + 1].y; v[6] += x[2 * r + 1].z; v[7] += x[2 * r + 1].w;
+          }
+        }
+      }
     }
   };
   const unsigned pos = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
