@@ -102,6 +102,27 @@ int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long l
                              long long ldy, int T, int I, int K, void* workspace, size_t ws_bytes,
                              b200_stream_t stream);
 
+/* RMSNorm (+ residual add) and the projection that consumes it, in one call:
+ *   s = x (+ residual) in fp32; residual_out = bf16(s)  (only with residual)
+ *   xn = bf16(norm_weight * (s / sqrt(mean(s^2) + eps)))   [T, K], row stride ldxn
+ *   y = xn * w^T (silu = 0: w [N, K], y [T, N]) or the gate_up projection
+ *       with SiLU-and-mul (silu = 1: w [N = 2I, K], y [T, I]).
+ * Replaces src/models/qwen3.py:162-168 (input_layernorm -> self_attn's
+ * qkv_proj, post_attention_layernorm -> mlp's gate_up_proj) =
+ * src/layers/layernorm.py:10-28 followed by src/layers/linear.py:74-75.
+ * By default the rms_norm kernel runs first, then the GEMM.  With the
+ * environment variable B200_FUSE_NORM=1, and when the GEMM runs on the
+ * persistent SM-pair kernel with every CTA resident, the norm rows are
+ * computed inside the GEMM launch instead (a grid barrier before its first
+ * activation loads, the weight loads already in flight; measured slower in
+ * the decode step).  Either way xn and residual_out hold the results.
+ * K <= 8192; workspace as for b200_linear (its flag words also hold the
+ * grid barrier). */
+int b200_rmsnorm_linear(const void* x, long long ldx, const void* residual, void* residual_out,
+                        const void* norm_weight, float eps, void* xn, long long ldxn, const void* w,
+                        long long ldw, void* y, long long ldy, int T, int N, int K, int silu,
+                        void* workspace, size_t ws_bytes, b200_stream_t stream);
+
 /* RowParallelLinear at tp > 1 in one launch: y = sum over ranks of
  * bf16(x_r * w_r^T (+ bias on rank 0)), the all-reduce of
  * src/layers/linear.py:169-173 (torch.distributed.all_reduce after F.linear)

@@ -553,9 +553,68 @@ int launch_pair(const GemmPlan& p, const CUtensorMap& tmW, const CUtensorMap& tm
   return check_launch(what);
 }
 
+// RMSNorm (+ residual add) ahead of a GEMM: x (+ residual) normalised by
+// weight into the GEMM's X operand (b200_rmsnorm_linear).
+struct NormIn {
+  const void* x;
+  long long ldx;
+  const void* residual;
+  void* residual_out;
+  const void* weight;
+  float eps;
+};
+
+// RMSNorm (+ residual add) rows on rms_norm_kernel (b200_rms_norm).
+int launch_rms_norm(const void* x, long long x_stride, const void* residual, const void* weight,
+                    void* out, long long out_stride, void* residual_out, int rows, int dim, float eps,
+                    cudaStream_t st) {
+  if (rows <= 0) return B200_OK;
+  if (dim <= 0 || dim % 8 || dim > 8 * 256 * 4)
+    return fail(B200_ERR_UNSUPPORTED, "rms_norm: dim %d must be a multiple of 8 and <= 8192", dim);
+  if (x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(out) || !aligned16(weight))
+    return fail(B200_ERR_INVALID, "rms_norm: rows must be 16-byte aligned");
+  if (residual && (!residual_out || !aligned16(residual) || !aligned16(residual_out)))
+    return fail(B200_ERR_INVALID, "rms_norm: residual needs an aligned residual_out");
+  const int nvec = dim / 8;
+  const int threads = nvec >= 256 ? 256 : max(32, round_up(nvec, 32));
+  const int vpt = (nvec + threads - 1) / threads;
+  auto X = static_cast<const __nv_bfloat16*>(x);
+  auto R = static_cast<const __nv_bfloat16*>(residual);
+  auto W = static_cast<const __nv_bfloat16*>(weight);
+  auto O = static_cast<__nv_bfloat16*>(out);
+  auto RO = static_cast<__nv_bfloat16*>(residual_out);
+#define B200_LAUNCH_NORM(V)                                                                      \
+  do {                                                                                           \
+    if (residual)                                                                                \
+      launch_ex(rms_norm_kernel<V, true>, dim3(rows), dim3(threads), 0, st, nullptr, 0, X,       \
+                x_stride, R, W, O, out_stride, RO, dim, eps);                                    \
+    else                                                                                         \
+      launch_ex(rms_norm_kernel<V, false>, dim3(rows), dim3(threads), 0, st, nullptr, 0, X,      \
+                x_stride, R, W, O, out_stride, RO, dim, eps);                                    \
+  } while (0)
+  if (vpt <= 1) B200_LAUNCH_NORM(1);
+  else if (vpt <= 2) B200_LAUNCH_NORM(2);
+  else B200_LAUNCH_NORM(4);
+#undef B200_LAUNCH_NORM
+  return check_launch("rms_norm_kernel");
+}
+
+// Word offset (in the pair workspace's flag area) of the fused RMSNorm's
+// grid barrier: arrivals, generation.
+constexpr int kNormBarrierWord = 1000;
+
+// Whether an eligible GEMM takes its RMSNorm inside its own launch: only
+// with B200_FUSE_NORM=1.  Measured slower in the Qwen3-8B decode step (21.7-
+// 21.8k against 22.4-22.5k tok/s, same box): the norm rows on four warps per
+// CTA plus the grid barrier take longer than the rms_norm launch they replace.
+bool fuse_norm_enabled() {
+  const char* e = getenv("B200_FUSE_NORM");
+  return e && *e == '1';
+}
+
 int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const void* bias, void* y,
              long long ldy, int T, int N, int K, bool silu, void* workspace, size_t ws_bytes,
-             cudaStream_t st) {
+             cudaStream_t st, const NormIn* norm = nullptr) {
   if (T <= 0) return B200_OK;
   if (N <= 0 || K <= 0) return fail(B200_ERR_INVALID, "linear: bad shape N=%d K=%d", N, K);
   if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K)
@@ -587,6 +646,7 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
   const bool csk_ok = !silu && pair_enabled() && workspace != nullptr && aligned16(workspace) &&
                       ws_bytes >= pair_workspace_bytes(ds->num_sms);
   bool csk_used = false;
+  bool all_resident = true;  // every CTA of the pair launch co-resident
   if (csk_ok && (csk_forced() || (!use_pair && T > kGemmBM))) {
     int prc = 0;
     bool resident = false;
@@ -595,7 +655,17 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
     if (cp.splits > 0 && (csk_forced() || (resident && cp.BN >= 192))) {
       pp = cp;
       pair = csk_used = true;
+      all_resident = resident;
     }
+  }
+  // RMSNorm fused into the launch (a grid barrier between the rows and the
+  // first activation loads) only on the persistent pair kernel with every CTA
+  // resident; otherwise its own launch ahead of the GEMM
+  const bool fuse = norm != nullptr && pair && all_resident && fuse_norm_enabled();
+  if (norm != nullptr && !fuse) {
+    if (int r = launch_rms_norm(norm->x, norm->ldx, norm->residual, norm->weight, const_cast<void*>(x), ldx,
+                                norm->residual_out, T, K, norm->eps, st))
+      return r;
   }
   if (!csk_used && use_pair) {
     int prc = 0;
@@ -630,6 +700,17 @@ int run_gemm(const void* x, long long ldx, const void* w, long long ldw, const v
     a.grp_size = p.grp_size;
     a.csplit = p.csplit;
     a.err = ds->err;
+    if (fuse) {
+      a.nx = static_cast<const __nv_bfloat16*>(norm->x);
+      a.ldnx = norm->ldx;
+      a.nres = static_cast<const __nv_bfloat16*>(norm->residual);
+      a.nres_out = static_cast<__nv_bfloat16*>(norm->residual_out);
+      a.nw = static_cast<const __nv_bfloat16*>(norm->weight);
+      a.neps = norm->eps;
+      a.nxo = static_cast<__nv_bfloat16*>(const_cast<void*>(x));
+      a.ldnxo = ldx;
+      a.gbar = static_cast<unsigned*>(workspace) + kNormBarrierWord;
+    }
     // outputs by TMA tensor stores: box of 32 features x 128 tokens, 64-byte
     // swizzle (the kernel's staging layout)
     CUtensorMap tmY;
@@ -908,39 +989,28 @@ int b200_linear_silu_and_mul(const void* x, long long ldx, const void* w, long l
                   reinterpret_cast<cudaStream_t>(stream));
 }
 
+int b200_rmsnorm_linear(const void* x, long long ldx, const void* residual, void* residual_out,
+                        const void* norm_weight, float eps, void* xn, long long ldxn, const void* w,
+                        long long ldw, void* y, long long ldy, int T, int N, int K, int silu,
+                        void* workspace, size_t ws_bytes, b200_stream_t stream) {
+  if (T <= 0) return B200_OK;
+  if (!x || !xn || !norm_weight || !w || !y)
+    return fail(B200_ERR_INVALID, "rmsnorm_linear: null pointer");
+  if (K <= 0 || K % 8 || K > 8192 || ldx % 8 || ldxn % 8 || ldx < K || ldxn < K || !aligned16(x) ||
+      !aligned16(xn) || !aligned16(norm_weight))
+    return fail(B200_ERR_INVALID, "rmsnorm_linear: K=%d (<= 8192, multiple of 8) and 16-byte aligned rows", K);
+  if (residual && (!residual_out || !aligned16(residual) || !aligned16(residual_out)))
+    return fail(B200_ERR_INVALID, "rmsnorm_linear: residual needs an aligned residual_out");
+  NormIn nrm{x, ldx, residual, residual ? residual_out : nullptr, norm_weight, eps};
+  return run_gemm(xn, ldxn, w, ldw, nullptr, y, ldy, T, N, K, silu != 0, workspace, ws_bytes,
+                  reinterpret_cast<cudaStream_t>(stream), &nrm);
+}
+
 int b200_rms_norm(const void* x, long long x_stride, const void* residual, const void* weight,
                   void* out, long long out_stride, void* residual_out, int rows, int dim, float eps,
                   b200_stream_t stream) {
-  if (rows <= 0) return B200_OK;
-  if (dim <= 0 || dim % 8 || dim > 8 * 256 * 4)
-    return fail(B200_ERR_UNSUPPORTED, "rms_norm: dim %d must be a multiple of 8 and <= 8192", dim);
-  if (x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(out) || !aligned16(weight))
-    return fail(B200_ERR_INVALID, "rms_norm: rows must be 16-byte aligned");
-  if (residual && (!residual_out || !aligned16(residual) || !aligned16(residual_out)))
-    return fail(B200_ERR_INVALID, "rms_norm: residual needs an aligned residual_out");
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int nvec = dim / 8;
-  const int threads = nvec >= 256 ? 256 : max(32, round_up(nvec, 32));
-  const int vpt = (nvec + threads - 1) / threads;
-  auto X = static_cast<const __nv_bfloat16*>(x);
-  auto R = static_cast<const __nv_bfloat16*>(residual);
-  auto W = static_cast<const __nv_bfloat16*>(weight);
-  auto O = static_cast<__nv_bfloat16*>(out);
-  auto RO = static_cast<__nv_bfloat16*>(residual_out);
-#define B200_LAUNCH_NORM(V)                                                                      \
-  do {                                                                                           \
-    if (residual)                                                                                \
-      launch_ex(rms_norm_kernel<V, true>, dim3(rows), dim3(threads), 0, st, nullptr, 0, X,       \
-                x_stride, R, W, O, out_stride, RO, dim, eps);                                    \
-    else                                                                                         \
-      launch_ex(rms_norm_kernel<V, false>, dim3(rows), dim3(threads), 0, st, nullptr, 0, X,      \
-                x_stride, R, W, O, out_stride, RO, dim, eps);                                    \
-  } while (0)
-  if (vpt <= 1) B200_LAUNCH_NORM(1);
-  else if (vpt <= 2) B200_LAUNCH_NORM(2);
-  else B200_LAUNCH_NORM(4);
-#undef B200_LAUNCH_NORM
-  return check_launch("rms_norm_kernel");
+  return launch_rms_norm(x, x_stride, residual, weight, out, out_stride, residual_out, rows, dim, eps,
+                         reinterpret_cast<cudaStream_t>(stream));
 }
 
 int b200_qk_norm_rope_store(const void* q_in, long long q_in_stride, const void* k_in,

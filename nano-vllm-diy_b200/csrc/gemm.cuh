@@ -92,6 +92,20 @@ struct GemmArgs {
   int sched;
   int grp_whole, grp_split, grp_size;
   int kstep;           // SM-pair kernel: 64-wide K blocks per ring stage (1 or 2)
+  // RMSNorm (+ residual add) of the activations fused ahead of the GEMM
+  // (SM-pair kernel with every CTA co-resident; gbar == nullptr: off): rows
+  // [0, T) of nx (+ nres) are normalised by nw into nxo, the X operand's
+  // rows; nres_out receives bf16(nx + nres).  Then a grid barrier, then the
+  // activation loads.
+  const __nv_bfloat16* nx;
+  long long ldnx;
+  const __nv_bfloat16* nres;   // nullptr: plain RMSNorm
+  __nv_bfloat16* nres_out;
+  const __nv_bfloat16* nw;
+  float neps;
+  __nv_bfloat16* nxo;
+  long long ldnxo;
+  unsigned* gbar;              // [2] arrivals, generation (zero-initialised workspace)
   int csplit;          // 2: cluster split-K (clusters of 2 pairs, one tile each, K halves
                        // reduced through distributed shared memory); 0: off
   unsigned* err;

@@ -243,6 +243,91 @@ __host__ __device__ inline bool pair_next_seg(int sched, long long tiles, int nu
 // counters in the flag area (the partial-ready flags use words [0, 2 pairs)).
 constexpr int kGrpDoneOffset = 512;
 
+// One row of the fused RMSNorm prologue (GemmArgs::gbar) on the 128
+// epilogue threads `et`: s = x (+ res) in fp32, res_out = bf16(s), out =
+// bf16(w * (s * 1/sqrt(mean(s^2) + eps))) -- the rounding points of
+// rms_norm_kernel (src/layers/layernorm.py:10-28).  Two passes over the row
+// (sum of squares, then the outputs) keep the registers of the GEMM's
+// epilogue free; `s_red` holds the 4 warps' partial sums.
+__device__ __forceinline__ void norm_row_128(const GemmArgs& p, int row, int et, float* s_red) {
+  const int nvec = p.K >> 3;
+  const __nv_bfloat16* xr = p.nx + (size_t)row * p.ldnx;
+  const __nv_bfloat16* rr = p.nres != nullptr ? p.nres + (size_t)row * p.K : nullptr;
+  auto load_sum = [&](int vi, float (&sv)[8]) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(xr + vi * 8);
+    const uint32_t* rw = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = unpack_bf16x2(rw[k]);
+      sv[2 * k] = f.x;
+      sv[2 * k + 1] = f.y;
+    }
+    if (rr != nullptr) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(rr + vi * 8);
+      const uint32_t* rp = reinterpret_cast<const uint32_t*>(&rv);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16x2(rp[k]);
+        sv[2 * k] = __fadd_rn(sv[2 * k], f.x);
+        sv[2 * k + 1] = __fadd_rn(sv[2 * k + 1], f.y);
+      }
+    }
+  };
+  float ss = 0.f;
+  for (int vi = et; vi < nvec; vi += 128) {
+    float sv[8];
+    load_sum(vi, sv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += sv[k] * sv[k];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((et & 31) == 0) s_red[et >> 5] = ss;
+  epi_bar_sync();
+  const float tot = ((s_red[0] + s_red[1]) + s_red[2]) + s_red[3];
+  const float inv = 1.0f / sqrtf(__fadd_rn(tot / (float)p.K, p.neps));
+  for (int vi = et; vi < nvec; vi += 128) {
+    float sv[8];
+    load_sum(vi, sv);
+    const uint4 wv = *reinterpret_cast<const uint4*>(p.nw + vi * 8);
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 o, so;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+    uint32_t* sp = reinterpret_cast<uint32_t*>(&so);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 wf = unpack_bf16x2(wp[k]);
+      op[k] = pack_bf16x2(__fmul_rn(wf.x, __fmul_rn(sv[2 * k], inv)), __fmul_rn(wf.y, __fmul_rn(sv[2 * k + 1], inv)));
+      sp[k] = pack_bf16x2(sv[2 * k], sv[2 * k + 1]);
+    }
+    if (rr != nullptr) *reinterpret_cast<uint4*>(p.nres_out + (size_t)row * p.K + vi * 8) = so;
+    *reinterpret_cast<uint4*>(p.nxo + (size_t)row * p.ldnxo + vi * 8) = o;
+  }
+  epi_bar_sync();  // s_red is reused by the next row
+}
+
+// Grid-wide barrier of a launch whose CTAs are all co-resident: gbar[0]
+// counts arrivals, gbar[1] is a generation number; the last CTA to arrive
+// resets the count and advances the generation.  Bounded (kWaitLimitNs).
+__device__ __forceinline__ bool grid_barrier(unsigned* gbar, unsigned nctas, unsigned* err) {
+  const unsigned gen = ld_acquire_gpu(gbar + 1);
+  __threadfence();
+  if (atomicAdd(gbar, 1u) == nctas - 1u) {
+    atomicExch(gbar, 0u);
+    __threadfence();
+    st_release_gpu(gbar + 1, gen + 1u);
+    return true;
+  }
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_gpu(gbar + 1) == gen) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      raise_error(err, ERR_PEER_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Partial tiles are [NP/32 chunks] of 16 KiB, each [8][128 tokens][4
 // features] fp32: a thread's 32 columns of a chunk are 8 float4 at stride
 // 2 KiB, so a warp's accesses are 512 contiguous bytes.  A finisher streams
@@ -277,7 +362,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_full = empty + kGemmMaxStages;   // [2] per CTA
   uint64_t* acc_empty = acc_full + 2;            // [2] used in the leader
   uint64_t* fix_bar = acc_empty + 2;             // [kFixSlots] stream-K partial loads
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fix_bar + kFixSlots);
+  uint64_t* norm_bar = fix_bar + kFixSlots;      // fused RMSNorm rows of this CTA written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(norm_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -320,6 +406,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(&acc_empty[0], 2);  // one release from each CTA's epilogue
     mbar_init(&acc_empty[1], 2);
     for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
+    mbar_init(norm_bar, 128);  // the epilogue threads
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -383,6 +470,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       griddep_wait();
       griddep_launch_dependents();
+      if (p.gbar != nullptr) {
+        // fused RMSNorm: this CTA's rows are written (the epilogue threads
+        // arrive after their stores); publish them and wait for every CTA's
+        // before the first activation load.  A timeout is recorded and the
+        // loads go ahead (the results are then flagged, never a hang).
+        mbar_wait(norm_bar, 0u, p.err);
+        grid_barrier(p.gbar, gridDim.x, p.err);
+        fence_proxy_async_global();
+      }
       while (ok && next_seg(su, sk, sg)) {
         const int kbb = sg.kbb, kbe = sg.kbe;
         const int mt = (int)(sg.tile / p.tiles_t);
@@ -467,6 +563,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (csk) cluster_arrive();  // this warp is done with the ring (cluster split-K)
   } else {
     // ---- epilogue warps 2..5: TMEM lane quarters 2,3,0,1; thread = token
+    if (p.gbar != nullptr) {
+      // fused RMSNorm first: rows blockIdx.x, + gridDim.x, ... of the
+      // activations, while the producer's first weight loads are in flight
+      __shared__ float s_nred[4];
+      for (int r = blockIdx.x; r < p.T; r += gridDim.x) norm_row_128(p, r, (int)threadIdx.x - 64, s_nred);
+      __threadfence();
+      mbar_arrive(norm_bar);
+    }
     const int q = warp & 3;
     const int row = q * 32 + lane;  // token inside this CTA's 128
     const bool lead_thread = (warp == 2 && lane == 0);

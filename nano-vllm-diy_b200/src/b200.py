@@ -42,6 +42,9 @@ _SIGNATURES = {
                      _c_void_p, _sz, _c_void_p], _i),
     "b200_linear_silu_and_mul": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _ll, _i, _i, _i,
                                   _c_void_p, _sz, _c_void_p], _i),
+    "b200_rmsnorm_linear": ([_c_void_p, _ll, _c_void_p, _c_void_p, _c_void_p, _f, _c_void_p, _ll,
+                             _c_void_p, _ll, _c_void_p, _ll, _i, _i, _i, _i, _c_void_p, _sz,
+                             _c_void_p], _i),
     "b200_linear_allreduce": ([_c_void_p, _ll, _c_void_p, _ll, _c_void_p, _i, _i, _i, _i, _i,
                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _ll, _ll, _ll, _i,
                                _c_void_p], _i),
@@ -266,6 +269,55 @@ def linear_silu_and_mul(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | No
                                         y2.stride(0), T, I, K, _p(ws), ws.numel(), _stream()),
            "b200_linear_silu_and_mul")
     return out
+
+
+def rmsnorm_linear(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, w: torch.Tensor,
+                   residual: torch.Tensor | None = None, silu: bool = False):
+    """RMSNorm of x (+ residual) followed by the projection that consumes it:
+    y = norm(x [+ residual]) @ w.T, or with silu=True the gate_up projection
+    silu(n @ w[:I].T) * (n @ w[I:].T).  Returns y, or (y, x + residual) with a
+    residual, as RMSNorm.forward then the linear layer would
+    (src/models/qwen3.py:162-168).  The rms_norm kernel then the GEMM; with
+    B200_FUSE_NORM=1 one launch where the GEMM runs on the persistent SM-pair
+    kernel."""
+    lib = load_library()
+    _cuda(x, norm_weight, w, residual)
+    _bf16(x, norm_weight, w, residual)
+    K = x.shape[-1]
+    N = w.shape[0]
+    if w.shape[1] != K or norm_weight.shape != (K,):
+        raise ValueError(f"rmsnorm_linear: x has K={K}, weight {tuple(w.shape)}, "
+                         f"norm weight {tuple(norm_weight.shape)}")
+    if w.stride(-1) != 1:
+        raise ValueError("rmsnorm_linear: weight rows must be contiguous")
+    if silu and (N % 2 or (N // 2) % 64):
+        # widths the fused SiLU epilogue does not pair: two steps
+        if residual is None:
+            return linear_silu_and_mul(rms_norm(x, norm_weight, eps), w)
+        n, r = rms_norm(x, norm_weight, eps, residual=residual)
+        return linear_silu_and_mul(n, w), r
+    x2 = x.reshape(-1, K)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    T = x2.shape[0]
+    res_out = None
+    if residual is not None:
+        if residual.shape != x.shape:
+            raise ValueError(f"rmsnorm_linear: residual {tuple(residual.shape)}, x {tuple(x.shape)}")
+        residual = residual.reshape(-1, K).contiguous()
+        res_out = torch.empty(T, K, dtype=x.dtype, device=x.device)
+    xn = torch.empty(T, K, dtype=x.dtype, device=x.device)
+    width = N // 2 if silu else N
+    y = torch.empty(T, width, dtype=x.dtype, device=x.device)
+    ws = _gemm_workspace(x.device)
+    _check(lib.b200_rmsnorm_linear(_p(x2), x2.stride(0), _p(residual), _p(res_out), _p(norm_weight),
+                                   float(eps), _p(xn), xn.stride(0), _p(w), w.stride(0), _p(y), y.stride(0),
+                                   T, N, K, int(silu), _p(ws), ws.numel(), _stream()),
+           "b200_rmsnorm_linear")
+    y = y.view(*x.shape[:-1], width)
+    if residual is None:
+        return y
+    return y, res_out.view(x.shape)
 
 
 ERR_UNSUPPORTED = -2

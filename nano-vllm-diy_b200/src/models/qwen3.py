@@ -57,8 +57,12 @@ class Qwen3Attention(nn.Module):
             self.q_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
             self.k_norm = RMSNorm(self.head_dim, eps=rms_norm_eps)
 
-    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor, ctx: Context) -> torch.Tensor:
-        qkv = self.qkv_proj(hidden_states)
+    def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor | None, ctx: Context,
+                qkv: torch.Tensor | None = None) -> torch.Tensor:
+        """`qkv`: the qkv projection already computed (the decoder layer fuses
+        it with the input RMSNorm); else it is computed from hidden_states."""
+        if qkv is None:
+            qkv = self.qkv_proj(hidden_states)
         T = qkv.shape[0]
         q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
         q = q.view(T, self.num_heads, self.head_dim)
@@ -91,9 +95,12 @@ class Qwen3MLP(nn.Module):
         assert hidden_act == "silu"
         self.act_fn = SiluAndMul()
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        # gate_up GEMM with silu(gate) * up in the epilogue
-        act = b200.linear_silu_and_mul(x, self.gate_up_proj.weight)
+    def forward(self, x: torch.Tensor | None, act: torch.Tensor | None = None) -> torch.Tensor:
+        """`act`: silu(gate) * up already computed (the decoder layer fuses the
+        gate_up projection with the post-attention RMSNorm)."""
+        if act is None:
+            # gate_up GEMM with silu(gate) * up in the epilogue
+            act = b200.linear_silu_and_mul(x, self.gate_up_proj.weight)
         return self.down_proj(act)
 
 
@@ -121,13 +128,28 @@ class Qwen3DecoderLayer(nn.Module):
 
     def forward(self, positions: torch.Tensor, hidden_states: torch.Tensor,
                 residual: torch.Tensor | None, ctx: Context) -> tuple[torch.Tensor, torch.Tensor]:
-        if residual is None:
-            hidden_states, residual = self.input_layernorm(hidden_states), hidden_states
+        # The layer order of the reference (src/models/qwen3.py:162-168), with
+        # each RMSNorm handed to the projection that consumes it
+        # (b200.rmsnorm_linear: two launches, or one with B200_FUSE_NORM=1).
+        attn, mlp = self.self_attn, self.mlp
+        n1, n2 = self.input_layernorm, self.post_attention_layernorm
+        if attn.qkv_bias:  # the fused call carries no bias
+            if residual is None:
+                hidden_states, residual = n1(hidden_states), hidden_states
+            else:
+                hidden_states, residual = n1(hidden_states, residual)
+            hidden_states = attn(positions, hidden_states, ctx)
         else:
-            hidden_states, residual = self.input_layernorm(hidden_states, residual)
-        hidden_states = self.self_attn(positions, hidden_states, ctx)
-        hidden_states, residual = self.post_attention_layernorm(hidden_states, residual)
-        hidden_states = self.mlp(hidden_states)
+            if residual is None:
+                qkv = b200.rmsnorm_linear(hidden_states, n1.weight, n1.eps, attn.qkv_proj.weight)
+                residual = hidden_states
+            else:
+                qkv, residual = b200.rmsnorm_linear(hidden_states, n1.weight, n1.eps, attn.qkv_proj.weight,
+                                                    residual=residual)
+            hidden_states = attn(positions, None, ctx, qkv=qkv)
+        act, residual = b200.rmsnorm_linear(hidden_states, n2.weight, n2.eps, mlp.gate_up_proj.weight,
+                                            residual=residual, silu=True)
+        hidden_states = mlp(None, act=act)
         return hidden_states, residual
 
 

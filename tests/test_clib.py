@@ -64,6 +64,16 @@ def test_invalid_arguments_fail_before_any_launch():
     rc = lib.b200_step_metadata(ctypes.c_void_p(16), None, 0, 4, 0, ctypes.c_void_p(16), None,
                                 ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), None)
     assert rc == -1
+    # RMSNorm + projection: the norm width (K) must be a multiple of 8, and a
+    # residual needs somewhere to write the sum
+    rc = lib.b200_rmsnorm_linear(ctypes.c_void_p(16), 12, None, None, ctypes.c_void_p(16), 1e-6,
+                                 ctypes.c_void_p(16), 12, ctypes.c_void_p(16), 12, ctypes.c_void_p(16),
+                                 16, 4, 16, 12, 0, None, 0, None)
+    assert rc == -1
+    rc = lib.b200_rmsnorm_linear(ctypes.c_void_p(16), 16, ctypes.c_void_p(16), None,
+                                 ctypes.c_void_p(16), 1e-6, ctypes.c_void_p(16), 16, ctypes.c_void_p(16),
+                                 16, ctypes.c_void_p(16), 16, 4, 16, 16, 0, None, 0, None)
+    assert rc == -1 and b"residual_out" in lib.b200_last_error()
     # the fused all-reduce's plan query rejects a bad shape without a device call
     ok = ctypes.c_int(7)
     rc = lib.b200_linear_allreduce_supported(256, 4100, 4096, 2, 512, 4096, 4096, ctypes.byref(ok))
