@@ -34,6 +34,7 @@ def randn(*s, std=1.0, seed=0):
 GEMM_SHAPES = [
     (1, 128, 64), (7, 384, 1024), (32, 4096, 4096), (100, 1000, 512), (256, 6144, 4096),
     (256, 4096, 12288), (300, 1024, 4096), (1000, 2048, 1024), (64, 18992, 256), (129, 256, 4104),
+    (256, 1536, 4096), (256, 768, 4096),  # qkv per rank at tp 4 / 8: cluster split-K
 ]
 
 
