@@ -36,8 +36,10 @@
 namespace b200 {
 
 constexpr int kDecHD = 128;
-constexpr int kDecItem = 512;     // tokens per work item (may span pages)
-constexpr int kDecItemPages = 4;  // block-table entries an item can touch (pages >= 256 tokens)
+constexpr int kDecItem = 512;        // tokens per work item (may span pages); sizes the workspace
+constexpr int kDecItemLong = 1024;   // tokens per item when the batch's mean context is long
+constexpr int kDecLongMean = 2048;   // mean context (keys per sequence) from which items are long
+constexpr int kDecItemPages = 4;     // block-table entries an item can touch (pages >= 256 tokens)
 constexpr int kDecTile = 32;      // tokens per pipeline stage
 constexpr int kDecStages = 3;
 constexpr int kDecWarps = 4;
@@ -134,16 +136,49 @@ __global__ void __launch_bounds__(128, 1)
   griddep_wait();
   griddep_launch_dependents();
 
-  // ---- plan: exclusive prefix sum of items per sequence (identical in every CTA)
+  // ---- plan: exclusive prefix sum of items per sequence (identical in every
+  // CTA).  Item length: 512 keys, or 1024 when the batch's mean context is at
+  // least kDecLongMean (half the per-item fixed work on long contexts; on
+  // short ones the longer last items would lengthen the tail).
+  int item_len = kDecItem;
   {
     const int tid = threadIdx.x;
     const int per = (a.B + 127) / 128;
     const int beg = min(a.B, tid * per), end = min(a.B, beg + per);
+    long long keys = 0;
+    int active = 0;
+    for (int b = beg; b < end; ++b) {
+      const int nq = a.cu_q[b + 1] - a.cu_q[b];
+      const int nk = a.cu_k[b + 1] - a.cu_k[b];
+      if (nq >= 1 && nk > 0) {
+        keys += nk;
+        ++active;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      keys += __shfl_xor_sync(0xffffffffu, keys, o);
+      active += __shfl_xor_sync(0xffffffffu, active, o);
+    }
+    __shared__ long long s_keys[kDecWarps];
+    if (lane == 0) {
+      s_keys[warp] = keys;
+      s_scan[warp] = active;
+    }
+    __syncthreads();
+    long long all_keys = 0;
+    int all_active = 0;
+    for (int w = 0; w < kDecWarps; ++w) {
+      all_keys += s_keys[w];
+      all_active += s_scan[w];
+    }
+    if (all_active > 0 && all_keys >= (long long)kDecLongMean * all_active) item_len = kDecItemLong;
+    __syncthreads();  // s_scan is reused by the scan below
     int local = 0;
     for (int b = beg; b < end; ++b) {
       const int nq = a.cu_q[b + 1] - a.cu_q[b];
       const int nk = a.cu_k[b + 1] - a.cu_k[b];
-      const int cnt = (nq >= 1 && nk > 0) ? (nk + kDecItem - 1) / kDecItem : 0;
+      const int cnt = (nq >= 1 && nk > 0) ? (nk + item_len - 1) / item_len : 0;
       s_start[b] = cnt;
       local += cnt;
     }
@@ -200,9 +235,9 @@ __global__ void __launch_bounds__(128, 1)
       if (s_start[mid] <= c) lo = mid; else hi = mid - 1;
     }
     const int b = lo;
-    const int j0 = (c - s_start[b]) * kDecItem;
+    const int j0 = (c - s_start[b]) * item_len;
     const int nk = a.cu_k[b + 1] - a.cu_k[b];
-    const int ntok_item = min(kDecItem, nk - j0);
+    const int ntok_item = min(item_len, nk - j0);
     // the block-table entries of the item's pages (one per lane 0..3)
     const int col0 = j0 / a.page;
     long long e = -1;
