@@ -481,7 +481,9 @@ def run_b200(args, rank: int, world: int):
     # run would have set the device error word
     dev_err = b200.device_error(clear=True)
     cpu = None
-    if rank == 0 and not args.no_cpu:
+    # the CPU port is timed at N = 1 only: under torchrun the other ranks would
+    # wait in the next collective for as long as rank 0 keeps the host's cores
+    if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(args.cpu_seconds, args.seed)
 
     if world > 1:
