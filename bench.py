@@ -105,6 +105,14 @@ class ClockSampler:
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+        # nvidia-smi can take a second or more to start (eight ranks starting
+        # it at once): wait, bounded, for its first sample so that the window
+        # really covers the steps that follow
+        t_end = time.time() + 5.0
+        while self.proc is not None and time.time() < t_end and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.05)
         return self
 
     def __exit__(self, *exc):
