@@ -34,3 +34,27 @@ def test_reference_arm_prints_the_contract_line():
     e2e = d["e2e"]
     assert e2e["unit"] == "tok/s" and e2e["value"] > 0
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_clock_summary_reads_the_sampled_reasons(tmp_path):
+    """The clock record that rides in the bench line: the median SM clock over
+    the loaded samples, the max clock, and every throttle reason seen active
+    (the driver rejects a run with a thermal or hardware slowdown)."""
+    sys.path.insert(0, REPO)
+    import bench
+    import torch
+    s = bench.ClockSampler(torch.device("cpu"))
+    s.path = str(tmp_path / "clocks.csv")
+    rows = ["0, 1965, 1965, 700.1, 0x0, Not Active, Not Active, Not Active, Not Active",
+            "0, 1950, 1965, 990.5, 0x4, Not Active, Not Active, Not Active, Active",
+            "0, 1935, 1965, 1000.2, 0x4, Not Active, Not Active, Not Active, Active",
+            "0, 210, 1965, 180.0, 0x1, Not Active, Not Active, Not Active, Not Active"]
+    with open(s.path, "w") as f:
+        f.write("\n".join(rows) + "\n")
+    d = s.summary()
+    assert d["sm_mhz"] == 1950 and d["sm_max_mhz"] == 1965 and d["samples"] == 4
+    assert d["reasons"] == ["sw_power_cap"]
+    # no file, or an empty one: marked unsampled rather than guessed
+    s.path = str(tmp_path / "empty.csv")
+    open(s.path, "w").close()
+    assert s.summary()["reasons"] == ["unsampled"]
